@@ -1,0 +1,568 @@
+"""Benchmark of the verify-pass hot path on B200 (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tsb|reference]
+
+Headline workload (the verify-pass qmm sweep): one
+step = the 4-bit g64 quantized matmul at every M in {1, 8, 16, 32, 64} on each
+of the shapes (N, K) = (6144, 5120), (34816, 5120), (5120, 17408): 15 calls.
+metric = algorithmic bytes of those calls (codes + scales/biases + x + y) per
+second, in TB/s. Inputs: seeded synthetic (x ~ N(0,1) bf16, W ~ N(0, 0.02)
+quantized); weights rotate through a pool of copies much larger than L2, so
+no call reads another call's weights from L2.
+
+At N > 1 GPUs (one process per GPU, torchrun) every weight is N-sharded by
+output rows and each layer's output is reassembled with an NCCL all-gather over
+NVLink inside the timed region (total work fixed: strong scaling).
+
+`--impl reference` times the reference's algorithm on the host CPU (the oracle
+port: dequantize + float32 matmul over all host threads; the reference's own
+kernels are Metal and cannot run here) on a bounded sample of the same
+workload, with the same metric and unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "mlx-tree-spec_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+SHAPES = ((6144, 5120), (34816, 5120), (5120, 17408))
+SWEEP_M = (1, 8, 16, 32, 64)
+METRIC = "4-bit qmm HBM TB/s (M<=64 verify sweep)"
+UNIT = "TB/s"
+
+
+def alg_bytes(m, n, k):
+    return n * k // 2 + n * (k // 64) * 4 + m * k * 2 + m * n * 2
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+class WeightPool:
+    """Per shape, `copies` distinct device copies of this rank's row shard."""
+
+    def __init__(self, world, rank, copies_for, seed=1000):
+        import torch
+
+        import tsb
+
+        self.shards = {}
+        for (n, k) in SHAPES:
+            ns = n // world
+            torch.manual_seed(seed + n + k)
+            wf = torch.randn(n, k, device="cuda") * 0.02
+            wq, s, b = tsb.quantize(wf[rank * ns:(rank + 1) * ns])
+            del wf
+            c = copies_for(ns, k)
+            self.shards[(n, k)] = [(wq, s, b)] + [(wq.clone(), s.clone(), b.clone()) for _ in range(c - 1)]
+        torch.cuda.synchronize()
+
+
+def copies_needed(ns, k, l2_bytes=126 * 2**20, factor=2.5):
+    per = ns * k // 2 + ns * (k // 64) * 4
+    return max(5, int(-(-factor * l2_bytes // per)))
+
+
+# ------------------------------------------------------------------ tsb arm
+
+def run_tsb(args):
+    import numpy as np
+    import torch
+
+    import tsb
+    from tsb import dist as tdist
+    from tsb import ops
+
+    world, rank, local = dist_setup()
+    hbm_peak, bf16_peak, peak_src = load_peaks()
+    lib = tsb.load_library()
+    pool = WeightPool(world, rank, copies_needed)
+    calls = [(m, n, k) for m in SWEEP_M for (n, k) in SHAPES]
+    total_bytes = sum(alg_bytes(m, n, k) for (m, n, k) in calls)
+
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    xs = {(m, k): torch.randn(m, k, device="cuda", generator=gen).to(torch.bfloat16)
+          for m in SWEEP_M for k in {k for _, k in SHAPES}}
+    sharded = tdist.ShardedQMM(world, rank) if world > 1 else None
+    ys = {(m, n): torch.empty(m, n, dtype=torch.bfloat16, device="cuda") for (m, n, k) in calls}
+
+    def launch(m, n, k, copy, y=None):
+        wq, s, b = pool.shards[(n, k)][copy % len(pool.shards[(n, k)])]
+        x = xs[(m, k)]
+        out = ys[(m, n)] if y is None else y
+        if sharded is None:
+            return ops.quantized_matmul_into(x, wq, s, b, out, n)
+        return sharded.forward_into(x, wq, s, b, out)
+
+    # one step = the 15 calls, each shape cycling through its copies
+    def step(offset=0):
+        used = {}
+        for (m, n, k) in calls:
+            c = used.get((n, k), 0)
+            used[(n, k)] = c + 1
+            launch(m, n, k, c + offset)
+
+    # warm-up (eager; sets kernel attributes, checks every call runs)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+
+    # CUDA graph of one step (kernel launches only; collectives use NCCL in-graph)
+    g = torch.cuda.CUDAGraph()
+    s_cap = torch.cuda.Stream()
+    s_cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s_cap):
+        step(0)  # warm the side stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s_cap):
+            step(0)
+    torch.cuda.current_stream().wait_stream(s_cap)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        g.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = t0.elapsed_time(t1) / args.steps
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world)
+    value = total_bytes / (ms * 1e-3) / 1e12
+
+    # per-call device time (graphs rotating through distinct weight copies)
+    per_call = {}
+    qmm_kernel_us = 0.0
+    for (m, n, k) in calls:
+        reps = len(pool.shards[(n, k)])
+        gc = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s_cap):
+            with torch.cuda.graph(gc, stream=s_cap):
+                for c in range(reps):
+                    launch(m, n, k, c)
+        torch.cuda.current_stream().wait_stream(s_cap)
+        gc.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        loops = 10
+        e0.record()
+        for _ in range(loops):
+            gc.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (loops * reps)
+        us = max_over_ranks(us, world)
+        per_call[f"M{m}_{n}x{k}"] = {"us": round(us, 3),
+                                      "GB/s": round(alg_bytes(m, n, k) / (us * 1e-6) / 1e9, 1)}
+        qmm_kernel_us += us
+        del gc
+    achieved_gbs = total_bytes / (qmm_kernel_us * 1e-6) / 1e9
+
+    # end to end through the public API: pinned host x in, y back to pinned host
+    host_x = {key: t.cpu().pin_memory() for key, t in xs.items()}
+    host_y = {key: torch.empty(t.shape, dtype=t.dtype).pin_memory() for key, t in ys.items()}
+    h2d = sum(m * k * 2 for (m, n, k) in calls)
+    d2h = sum(m * n * 2 for (m, n, k) in calls)
+
+    def e2e_step():
+        used = {}
+        for (m, n, k) in calls:
+            c = used.get((n, k), 0)
+            used[(n, k)] = c + 1
+            wq, s, b = pool.shards[(n, k)][c % len(pool.shards[(n, k)])]
+            xd = host_x[(m, k)].to("cuda", non_blocking=True)
+            if sharded is None:
+                y = tsb.quantized_matmul(xd, wq, s, b)
+            else:
+                y = sharded.forward(xd, wq, s, b)
+            host_y[(m, n)].copy_(y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(2):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max(e0.elapsed_time(e1), (time.perf_counter() - w0) * 1e3) / args.steps
+    e2e_ms = max_over_ranks(e2e_ms, world)
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e12
+
+    launches_per_step = 2 * len(calls)  # x-fragment prep + qmm kernel per call
+
+    secondary = {}
+    if args.secondary and rank == 0 and world == 1:
+        secondary = run_secondary(pool, xs, hbm_peak, bf16_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        cpu = cpu_baseline_sample()
+
+    traffic = read_traffic()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "verify-pass qmm sweep: M in {1,8,16,32,64} x (N,K) in "
+                                   "{(6144,5120),(34816,5120),(5120,17408)}, 4-bit g64 MLX format",
+                       "bytes_per_step": total_bytes, "calls_per_step": len(calls),
+                       "l2": "inputs larger than L2: rotating weight pool, >= 2.5 x 126 MiB of distinct copies per shape",
+                       "parallelism": f"N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "timing": "CUDA graph of one step, CUDA events"},
+            "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms, 4), "path": "tsb.quantized_matmul, pinned host x/y, eager"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,
+                         "kernel": "qmm_small_kernel (+ x prep)", "peak_source": peak_src,
+                         "basis": "sum of algorithmic bytes / sum of per-call device time over the 15 calls"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "per_call": per_call,
+        }
+        if secondary:
+            line["secondary"] = secondary
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def read_traffic():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "qmm_small_sweep_traffic.txt")
+    try:
+        for ln in open(p):
+            if ln.startswith("traffic_bytes_per_step:"):
+                return float(ln.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def time_graph(fn, loops=10):
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(loops):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / loops  # us per replay
+
+
+def run_secondary(pool, xs, hbm_peak, bf16_peak):
+    """M=128 sweep, prefill M=4096, tree attention (config 4): reported beside
+    the headline, not part of it."""
+    import torch
+
+    import tsb
+    from tsb import ops
+
+    out = {}
+    # M = 128 (tensor-bound past M ~ 70)
+    for (n, k) in SHAPES:
+        x = torch.randn(128, k, device="cuda").to(torch.bfloat16)
+        y = torch.empty(128, n, dtype=torch.bfloat16, device="cuda")
+        copies = pool.shards[(n, k)]
+
+        def f():
+            for (wq, s, b) in copies:
+                ops.quantized_matmul_into(x, wq, s, b, y, n)
+
+        us = time_graph(f) / len(copies)
+        out[f"qmm_M128_{n}x{k}"] = {"us": round(us, 2), "TFLOP/s": round(2 * 128 * n * k / us / 1e6, 1),
+                                    "GB/s": round(alg_bytes(128, n, k) / us / 1e3, 1)}
+    # prefill M = 4096
+    for (n, k) in ((34816, 5120), (5120, 17408)):
+        x = torch.randn(4096, k, device="cuda").to(torch.bfloat16)
+        y = torch.empty(4096, n, dtype=torch.bfloat16, device="cuda")
+        wq, s, b = pool.shards[(n, k)][0]
+        us = time_graph(lambda: ops.quantized_matmul_into(x, wq, s, b, y, n), loops=3)
+        tf = 2 * 4096 * n * k / us / 1e6
+        out[f"prefill_M4096_{n}x{k}"] = {"us": round(us, 1), "TFLOP/s": round(tf, 1),
+                                         "frac_of_bf16_peak": round(tf / bf16_peak, 4)}
+    # tree attention, config 4: T=32, 24q/4kv, D=256
+    from oracle import gen
+    import numpy as np
+
+    for (bsz, L, fmt) in ((1, 32768, "bf16"), (4, 8192, "bf16"), (1, 32768, "mlx_q8"), (4, 8192, "mlx_q8")):
+        t, hq, hkv, d = 32, 24, 4, 256
+        n_kv = L + t
+        caches = []
+        for i in range(4):  # rotate 4 caches so K/V are not L2-resident
+            kf = torch.randn(bsz, hkv, n_kv, d, device="cuda")
+            vf = torch.randn(bsz, hkv, n_kv, d, device="cuda")
+            if fmt == "bf16":
+                caches.append(tsb.KVCache(kf.to(torch.bfloat16), vf.to(torch.bfloat16), n_kv))
+            else:
+                kw, ks, kb = tsb.quantize_g64(kf)
+                vw, vs, vb = tsb.quantize_g64(vf)
+                caches.append(tsb.MLXQ8KVCache(kw, vw, ks, kb, vs, vb, n_kv))
+            del kf, vf
+        q = torch.randn(bsz, hq, t, d, device="cuda").to(torch.bfloat16)
+        parents = torch.from_numpy(np.stack([gen.tree_parents(np.random.default_rng(i), t) for i in range(bsz)])).cuda()
+
+        def f():
+            for c in caches:
+                tsb.tree_flash(q, c, d**-0.5, parents=parents)
+
+        us = time_graph(f) / len(caches)
+        row = 512 if fmt == "bf16" else 272
+        byts = bsz * n_kv * hkv * row * 2 + 2 * bsz * t * hq * d * 2
+        fl = 4.0 * bsz * t * hq * n_kv * d
+        out[f"attn_B{bsz}_L{L}_{fmt}"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1),
+                                          "TFLOP/s": round(fl / us / 1e6, 1),
+                                          "frac_hbm": round(byts / us / 1e3 / hbm_peak, 4)}
+        del caches
+    # unmasked FlashAttention comparator (torch SDPA, same shape, bf16)
+    try:
+        bsz, L, t, hq, hkv, d = 1, 32768, 32, 24, 4, 256
+        kk = [torch.randn(bsz, hq, L + t, d, device="cuda").to(torch.bfloat16) for _ in range(2)]
+        q = torch.randn(bsz, hq, t, d, device="cuda").to(torch.bfloat16)
+        us = time_graph(lambda: [torch.nn.functional.scaled_dot_product_attention(q, k_, k_) for k_ in kk]) / 2
+        out["sdpa_unmasked_B1_L32768_bf16_fullheads"] = {"us": round(us, 2), "note": "torch SDPA, K/V expanded to 24 heads"}
+        del kk
+    except Exception as e:  # pragma: no cover - comparator only
+        out["sdpa_unmasked"] = {"error": str(e)[:120]}
+    return out
+
+
+def cpu_baseline_sample():
+    """The oracle port on this host's cores: the 3 shapes at M=16 (one call each)."""
+    import numpy as np
+
+    from oracle import gen, qmm
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    tot_b, tot_t = 0, 0.0
+    for (n, k) in SHAPES:
+        x = gen.x_bf16(rng, 16, k)
+        wq = rng.integers(0, 2**32, size=(n, k // 8), dtype=np.uint64).astype(np.uint32)
+        s = np.full((n, k // 64), 0x3C00, dtype=np.uint16)  # bf16 0.0078125
+        b = np.full((n, k // 64), 0xBC80, dtype=np.uint16)
+        qmm.qmm_cpu(x[:1], wq[:256], s[:256], b[:256], threads)  # warm
+        t0 = time.perf_counter()
+        qmm.qmm_cpu(x, wq, s, b, threads)
+        tot_t += time.perf_counter() - t0
+        tot_b += alg_bytes(16, n, k)
+    return {"value": round(tot_b / tot_t / 1e12, 6), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": "oracle port (dequantize + f32 matmul), one M=16 call on each of the 3 shapes"}
+
+
+# ------------------------------------------------------------------ reference arm
+
+def run_reference(args):
+    """The reference's algorithm on the host CPU (oracle port), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import gen, qmm
+
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    # one M = 16 call per step, cycling through the three shapes
+    data = []
+    for (n, k) in SHAPES:
+        x = gen.x_bf16(rng, 16, k)
+        wq = rng.integers(0, 2**32, size=(n, k // 8), dtype=np.uint64).astype(np.uint32)
+        s = np.full((n, k // 64), 0x3C00, dtype=np.uint16)
+        b = np.full((n, k // 64), 0xBC80, dtype=np.uint16)
+        data.append((x, wq, s, b, alg_bytes(16, n, k)))
+    for i in range(args.warmup):
+        x, wq, s, b, _ = data[i % 3]
+        qmm.qmm_cpu(x, wq, s, b, threads)
+    tot_b, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        x, wq, s, b, nb = data[i % 3]
+        qmm.qmm_cpu(x, wq, s, b, threads)
+        tot_b += nb
+    dt = time.perf_counter() - t0
+    value = tot_b / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "verify-pass qmm sweep (bounded sample: one M=16 call per step, shapes cycled)",
+                   "note": "reference kernels are Metal (MLX/MTPLX), unavailable on this box; "
+                           "CPU port of its arithmetic"},
+        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "one M=16 qmm per step over the 3 shapes (dequantize + f32 matmul)"},
+        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["tsb", "reference"], default="tsb")
+    ap.add_argument("--no-secondary", dest="secondary", action="store_false")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_tsb(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+/*
+ * tsb.h — C ABI of libtsb.so, the B200 (sm_100a) verify-pass hot path of
+ * mlx-tree-spec: the MLX 4-bit affine quantized matmul and tree-mask flash
+ * attention over a long KV prefix.
+ *
+ * Conventions (mirroring the reference's operator contract):
+ *   - Every entry point returns an int status. TSB_OK on success.
+ *     TSB_EUNSUPPORTED means "decline": the shape or format is one this library
+ *     does not take, and the caller falls back, as the reference's kernels
+ *     return None (mlx-tree-spec src/mlx_tree_spec/tree_flash.py:165-172,
+ *     tree_verify.py:363-366). TSB_EINVAL is a contract violation (null or
+ *     misaligned pointer, inconsistent sizes), as the reference's asserts
+ *     (qmm_packed.py:113,227,375,705; tree_flash.py:113).
+ *   - All pointers are device pointers unless stated otherwise. Inputs are
+ *     read only. Nothing is allocated inside: scratch memory is passed by the
+ *     caller as (ws, ws_bytes), sized by the matching *_workspace_bytes().
+ *   - All work is enqueued on the caller's stream; calls are asynchronous and
+ *     stateless, so concurrent calls on different streams are safe as long as
+ *     their outputs and workspaces do not overlap.
+ *   - bf16 tensors are passed as `const void*` holding IEEE bfloat16 values.
+ */
+#ifndef TSB_H
+#define TSB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st *tsb_stream_t;
+
+enum {
+  TSB_OK = 0,
+  TSB_EUNSUPPORTED = 1, /* declined: caller falls back (tree_flash.py:165-172) */
+  TSB_EINVAL = 2,       /* contract violation: bad pointer, size or alignment */
+  TSB_ECUDA = 3,        /* CUDA runtime or launch error */
+  TSB_ETIMEOUT = 4,     /* a bounded device-side wait gave up */
+  TSB_EWORKSPACE = 5    /* workspace smaller than *_workspace_bytes() */
+};
+
+/* KV-cache formats read by tsb_tree_attn. */
+enum {
+  TSB_KV_BF16 = 0,       /* data bf16 [B,Hkv,cap,D]; scales = biases = NULL                */
+  TSB_KV_MLX_Q8_G64 = 1, /* data uint32 [B,Hkv,cap,D/4] (4 codes, low byte first);
+                            scales, biases bf16 [B,Hkv,cap,D/64]; value = s*q + b          */
+  TSB_KV_REF_Q8_ROW = 2  /* data int8 [B,Hkv,cap,D]; scales float [B,Hkv,cap]; biases NULL;
+                            value = q * s (mlx-tree-spec src/mlx_tree_spec/kv8.py:39-43)   */
+};
+
+/* Human-readable text of a status code (static storage). */
+const char *tsb_strerror(int status);
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int tsb_version(void);
+
+/* ------------------------------------------------------------------------
+ * Quantized matmul, MLX affine format, group 64, 4 bits.
+ *
+ * y[m, n] = sum_k x[m, k] * W[n, k],  W[n, k] = s[n, k/64] * q[n, k] + b[n, k/64]
+ *
+ * Replaces mx.quantized_matmul(x, w, scales, biases, transpose=True,
+ * group_size=64, bits=4) as called by the reference's patched
+ * nn.QuantizedLinear (mlx-tree-spec src/mlx_tree_spec/packed_linear.py:83-104,
+ * call site 97) and its launchers (qmm_packed.py:270-293 nax_kernel,
+ * 372-394 nax_multi_kernel, 529-557 _qmv_kernel, 701-725 prefill_kernel).
+ *
+ *   x      bf16 [M, K], row stride K
+ *   w      uint32 [N, K/8]: word c of row n holds k = 8c..8c+7, element i in
+ *          bits 4i..4i+3 (MLX layout, read directly, no repack)
+ *   scales bf16 [N, K/64];  biases bf16 [N, K/64]
+ *   y      bf16 [M, ldy] (ldy >= N; an N-shard may write into a wider buffer)
+ * Requirements: M >= 1, N % 128 == 0, K % 64 == 0, ldy % 8 == 0; x, w, y
+ * 16-byte aligned. Accumulation in float32. Declines (TSB_EUNSUPPORTED)
+ * other N/K granularities.
+ * ---------------------------------------------------------------------- */
+size_t tsb_qmm_workspace_bytes(int M, int N, int K);
+int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const void *biases, void *y,
+                  int M, int N, int K, int ldy, void *ws, size_t ws_bytes, tsb_stream_t stream);
+
+/* Bit-exact dequantization: out[n, k] = bf16_rne(fmaf(q, s, b)) as bf16 [N, K].
+ * Reference rule: `T(float(q) * s + b)` in qmm_packed.py:200,348,635.
+ * Requirements: K % 64 == 0. */
+int tsb_dequant_w4g64(const uint32_t *w, const void *scales, const void *biases, void *out,
+                      int N, int K, tsb_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Tree masks.
+ *
+ * parents int32 [B, T]: parent of each node (-1 for a root; otherwise an
+ * earlier node). bits uint64 [B, T]: bit j of node i set iff j is i or one of
+ * its ancestors. depth int32 [B, T] (nullable): 0 for roots. Replaces
+ * Tree.__init__/ancestor_bits (mlx-tree-spec src/mlx_tree_spec/tree_verify.py:
+ * 66-121, tree_flash.py:146-148), extended to forests. T <= 64. A parent that
+ * is neither -1 nor an earlier node yields bits = 0 and depth = -1 for that
+ * node (the reference asserts, tree_verify.py:71).
+ * ---------------------------------------------------------------------- */
+int tsb_tree_ancestor_bits(const int32_t *parents, int B, int T, uint64_t *bits, int32_t *depth,
+                           tsb_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Tree-mask flash attention (split-KV flash decoding with fused combine).
+ *
+ * out[b, h, t, :] = softmax_j(scale * q[b,h,t] . k[b,h/G,j] over visible j) . v
+ * with G = Hq / Hkv. Row j (0 <= j < n_kv) is visible to node t iff
+ * j < n_kv - tail, or bit (j - (n_kv - tail)) of the node's mask is set.
+ * The mask comes from `parents` (int32 [B, T], tail = T: the nodes' own K/V
+ * are the cache's last T valid rows) when non-NULL, computed inside the
+ * kernel; otherwise from `bits` (uint64 [B, T], any tail <= 64; tail 0 makes
+ * every row visible). Replaces tree_flash(queries, cache, scale, bits, tail,
+ * stats) (mlx-tree-spec src/mlx_tree_spec/tree_flash.py:151-196) and the q8
+ * path kv8.attention (kv8.py:162-188), without its bsz == 1 / n <= 16 /
+ * tail <= 64-only limits except tail <= 64.
+ *
+ *   q        bf16 [B, Hq, T, D]
+ *   k, v     per kv_format (see TSB_KV_*), kv_capacity rows per (b, head)
+ *   out      bf16 [B, Hq, T, D]
+ *   lse      float [B, Hq, T] (nullable): natural-log sum of exp of the
+ *            visible scaled scores (-inf for a node that sees nothing), the
+ *            statistic that lets more keys be merged in later (the block
+ *            max/sum of tree_flash(stats=True) collapsed to one block).
+ * Requirements: D == 256, Hq % Hkv == 0, 1 <= T <= 64, n_kv <= kv_capacity.
+ * ---------------------------------------------------------------------- */
+size_t tsb_tree_attn_workspace_bytes(int B, int T, int Hq, int Hkv, int D, int n_kv, int kv_format);
+int tsb_tree_attn(const void *q,
+                  const void *k, const void *k_scales, const void *k_biases,
+                  const void *v, const void *v_scales, const void *v_biases,
+                  int kv_format, const int32_t *parents, const uint64_t *bits,
+                  int B, int T, int Hq, int Hkv, int D, int n_kv, int tail, int kv_capacity,
+                  float scale, void *out, float *lse, void *ws, size_t ws_bytes, tsb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TSB_H */

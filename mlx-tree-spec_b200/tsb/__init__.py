@@ -1,0 +1,20 @@
+"""tsb: the B200-native verify-pass hot path of mlx-tree-spec.
+
+Operators (reference-facing, over torch CUDA tensors):
+  quantized_matmul, dequantize, ancestor_bits, tree_flash
+Containers: KVCache, Q8KVCache, MLXQ8KVCache
+Input makers: quantize, quantize_rows, quantize_g64
+Sharding: tsb.dist (N-sharded qmm with an NCCL all-gather)
+
+All compute runs in libtsb.so (sm_100a CUDA); importing the operators loads
+it and fails loudly if it is missing.
+"""
+
+from . import _lib
+from ._lib import (TSB_KV_BF16, TSB_KV_MLX_Q8_G64, TSB_KV_REF_Q8_ROW, TSBError,  # noqa: F401
+                   load as load_library)
+from .cache import KVCache, MLXQ8KVCache, Q8KVCache  # noqa: F401
+from .ops import ancestor_bits, dequantize, quantized_matmul, tree_flash, workspace  # noqa: F401
+from .quant import quantize, quantize_g64, quantize_rows  # noqa: F401
+
+__version__ = "0.1.0"

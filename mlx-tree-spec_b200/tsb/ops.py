@@ -1,0 +1,204 @@
+"""The reference-facing operators over torch CUDA tensors.
+
+Each function mirrors the call the reference makes on its hot path, with the
+same argument names and meaning:
+
+  quantized_matmul(x, w, scales, biases, transpose=True, group_size=64, bits=4)
+      = mx.quantized_matmul as called by the patched nn.QuantizedLinear
+        (mlx-tree-spec src/mlx_tree_spec/packed_linear.py:83-104, :97)
+  dequantize(w, scales, biases, group_size=64, bits=4)
+      = mx.dequantize (tests/test_units.py:108), bit-exact rule
+  ancestor_bits(parents)
+      = tree_flash.ancestor_bits over Tree.anc (tree_flash.py:146-148,
+        tree_verify.py:66-121)
+  tree_flash(queries, cache, scale, bits, tail=None, stats=False)
+      = tree_flash.tree_flash (tree_flash.py:151-196); also takes `parents=`
+        so the mask is built inside the kernel.
+
+Decline behaviour follows the reference: an unsupported shape or format
+returns None (the caller falls back), contract violations raise. All work is
+enqueued on torch's current CUDA stream; scratch memory comes from a per-device
+workspace owned here (the C ABI itself never allocates).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import TSB_EUNSUPPORTED, TSB_KV_BF16, TSB_KV_MLX_Q8_G64, TSB_KV_REF_Q8_ROW, check
+
+_WS: dict[int, torch.Tensor] = {}
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    """A per-device uint8 scratch buffer of at least nbytes (grown, never shrunk)."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    buf = _WS.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _WS[idx] = buf
+    return buf
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("tsb operators take CUDA tensors (there is no CPU path)")
+
+
+def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: int = 64, bits: int = 4,
+                     out: torch.Tensor | None = None):
+    """y = x @ dequantize(w, scales, biases).T for x (..., K) bf16.
+
+    w: uint32 (N, K/8) [torch.int32 or torch.uint32 storage]; scales, biases:
+    bf16 (N, K/64). Returns (..., N) bf16, or None when declined (the shape
+    or configuration is not one this kernel takes)."""
+    _require_cuda(x, w, scales, biases)
+    if not transpose or group_size != 64 or bits != 4:
+        return None
+    if x.dtype != torch.bfloat16 or scales.dtype != torch.bfloat16 or biases.dtype != torch.bfloat16:
+        return None
+    k = x.shape[-1]
+    n = w.shape[0]
+    if w.shape[-1] * 8 != k or scales.shape != (n, k // 64) or biases.shape != (n, k // 64):
+        raise ValueError(f"inconsistent shapes: x {tuple(x.shape)}, w {tuple(w.shape)}, scales {tuple(scales.shape)}")
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws_n = lib.tsb_qmm_workspace_bytes(m, n, k)
+    ws = workspace(ws_n, x.device)
+    st = lib.tsb_qmm_w4g64(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), m, n, k, n,
+                           _ptr(ws), ws.numel(), _stream(x))
+    if check(st, "tsb_qmm_w4g64") == TSB_EUNSUPPORTED:
+        return None
+    return out
+
+
+def quantized_matmul_into(x2, w, scales, biases, y, ldy: int):
+    """Low-level: x2 (M, K) contiguous -> y (an (M, ldy) buffer, N columns written).
+
+    Used by the N-sharded path to write a shard straight into a wider buffer."""
+    m, k = x2.shape
+    n = w.shape[0]
+    lib = _lib.load()
+    ws = workspace(lib.tsb_qmm_workspace_bytes(m, n, k), x2.device)
+    st = lib.tsb_qmm_w4g64(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(y), m, n, k, ldy,
+                           _ptr(ws), ws.numel(), _stream(x2))
+    return check(st, "tsb_qmm_w4g64")
+
+
+def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4):
+    """Bit-exact dequantization: bf16 (N, K) = bf16_rne(fmaf(q, s, b))."""
+    _require_cuda(w, scales, biases)
+    if group_size != 64 or bits != 4:
+        return None
+    n = w.shape[0]
+    k = w.shape[1] * 8
+    out = torch.empty((n, k), dtype=torch.bfloat16, device=w.device)
+    lib = _lib.load()
+    st = lib.tsb_dequant_w4g64(_ptr(w), _ptr(scales), _ptr(biases), _ptr(out), n, k, _stream(w))
+    if check(st, "tsb_dequant_w4g64") == TSB_EUNSUPPORTED:
+        return None
+    return out
+
+
+def ancestor_bits(parents, depth: bool = False):
+    """parents int32 (T,) or (B, T) on the GPU -> uint64 masks (as int64 storage),
+    and the node depths if asked."""
+    _require_cuda(parents)
+    p = parents.to(torch.int32)
+    squeeze = p.dim() == 1
+    p2 = p.reshape(1, -1) if squeeze else p
+    p2 = p2.contiguous()
+    b, t = p2.shape
+    bits = torch.empty((b, t), dtype=torch.int64, device=p.device)
+    dep = torch.empty((b, t), dtype=torch.int32, device=p.device) if depth else None
+    lib = _lib.load()
+    st = lib.tsb_tree_ancestor_bits(_ptr(p2), b, t, _ptr(bits), _ptr(dep), _stream(p2))
+    if check(st, "tsb_tree_ancestor_bits") == TSB_EUNSUPPORTED:
+        return None
+    if squeeze:
+        bits = bits[0]
+        dep = dep[0] if dep is not None else None
+    return (bits, dep) if depth else bits
+
+
+def _kv_planes(cache):
+    """(format, k, k_scales, k_biases, v, v_scales, v_biases) of a cache object."""
+    fmt = getattr(cache, "kv_format", None)
+    if fmt is None:
+        fmt = TSB_KV_REF_Q8_ROW if getattr(cache, "k_scale", None) is not None else TSB_KV_BF16
+    if fmt == TSB_KV_BF16:
+        return fmt, cache.keys, None, None, cache.values, None, None
+    if fmt == TSB_KV_REF_Q8_ROW:
+        return fmt, cache.keys, cache.k_scale, None, cache.values, cache.v_scale, None
+    if fmt == TSB_KV_MLX_Q8_G64:
+        return fmt, cache.keys, cache.k_scales, cache.k_biases, cache.values, cache.v_scales, cache.v_biases
+    raise ValueError(f"unknown kv format {fmt}")
+
+
+def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None, stats: bool = False,
+               parents=None):
+    """Tree-mask attention of `queries` (B, Hq, n, D) over `cache`.
+
+    cache: any object with keys/values (B, Hkv, capacity, ...) and `offset`
+    (valid rows, the nodes' own rows last), optionally k_scale/v_scale (the
+    reference's int8-row format) or kv_format = TSB_KV_MLX_Q8_G64 with
+    k_scales/k_biases/v_scales/v_biases. Visibility per the reference: node q
+    sees the rows before the last `tail` (default n) plus the tail rows set in
+    bits[q] (uint64 masks as int64, shape (n,) or (B, n); tail 0 = all rows).
+    With parents= (int32 (n,) or (B, n)) the masks are built in the kernel.
+
+    Returns out (B, Hq, n, D) bf16, or (out, maxs, sums) with stats=True where
+    maxs = log-sum-exp of each row's visible scores and sums = 1 (a single
+    block: merge with more keys as tree_verify.py:389-401 does), or None when
+    declined."""
+    fmt, k, ks, kb, v, vs, vb = _kv_planes(cache)
+    _require_cuda(queries, k, v)
+    if queries.dtype != torch.bfloat16:
+        return None
+    bsz, hq, n, d = queries.shape
+    hkv, cap = k.shape[1], k.shape[2]
+    n_kv = int(cache.offset)
+    if parents is not None:
+        p = parents.to(device=queries.device, dtype=torch.int32)
+        p = p.reshape(1, n).expand(bsz, n) if p.dim() == 1 else p
+        p = p.contiguous()
+        bits_t = None
+        tail_v = n
+    else:
+        if bits is None:
+            return None
+        bt = bits if isinstance(bits, torch.Tensor) else torch.tensor([int(b) if int(b) < 2**63 else int(b) - 2**64 for b in bits], dtype=torch.int64)
+        bt = bt.to(device=queries.device, dtype=torch.int64)
+        bt = bt.reshape(1, n).expand(bsz, n) if bt.dim() == 1 else bt
+        bits_t = bt.contiguous()
+        p = None
+        tail_v = n if tail is None else int(tail)
+    q = queries.contiguous()
+    out = torch.empty_like(q)
+    lse = torch.empty((bsz, hq, n), dtype=torch.float32, device=q.device) if stats else None
+    lib = _lib.load()
+    ws = workspace(lib.tsb_tree_attn_workspace_bytes(bsz, n, hq, hkv, d, n_kv, fmt), q.device)
+    st = lib.tsb_tree_attn(_ptr(q), _ptr(k), _ptr(ks), _ptr(kb), _ptr(v), _ptr(vs), _ptr(vb), fmt,
+                           _ptr(p), _ptr(bits_t), bsz, n, hq, hkv, d, n_kv, tail_v, cap, float(scale),
+                           _ptr(out), _ptr(lse), _ptr(ws), ws.numel(), _stream(q))
+    if check(st, "tsb_tree_attn") == TSB_EUNSUPPORTED:
+        return None
+    if stats:
+        return out, lse[..., None], torch.ones_like(lse)[..., None]
+    return out
