@@ -56,6 +56,14 @@ const char *tsb_strerror(int status);
 /* Library version, (major << 16) | (minor << 8) | patch. */
 int tsb_version(void);
 
+/* Synchronizes `stream`, then returns the first failure any kernel recorded on
+ * the device since the last reset: TSB_OK, or TSB_ETIMEOUT when a bounded
+ * device-side wait (pipeline barrier) gave up instead of hanging. The kernel
+ * that records it stops its work and returns, so the context stays usable.
+ * reset != 0 clears the record. No counterpart in the reference (its Metal
+ * kernels have no device-side waits). */
+int tsb_device_status(tsb_stream_t stream, int reset);
+
 /* ------------------------------------------------------------------------
  * Quantized matmul, MLX affine format, group 64, 4 bits.
  *

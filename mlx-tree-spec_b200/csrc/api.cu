@@ -1,5 +1,6 @@
-// Library-wide entry points: status strings, version, device facts.
-#include "common.cuh"
+// Library-wide entry points: status strings, version, device status, and the
+// host-side helpers shared by the kernels (SM count, TMA tensor maps).
+#include "sm100.cuh"
 
 namespace tsb {
 
@@ -16,7 +17,49 @@ int sm_count() {
   return cached[dev];
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t cols,
+                 uint64_t rows, uint64_t row_pitch_bytes, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return TSB_ECUDA;
+  (void)elem_bytes;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_pitch_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? TSB_OK : TSB_ECUDA;
+}
+
+unsigned int status_gemm(bool reset);
+
 }  // namespace tsb
+
+// Synchronizes `stream`, then reports the first device-side failure recorded
+// by any kernel since the last reset (TSB_OK if none): a bounded wait that ran
+// out (TSB_ETIMEOUT). reset != 0 clears the record.
+extern "C" int tsb_device_status(tsb_stream_t stream, int reset) {
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return TSB_ECUDA;
+  const unsigned int v = tsb::status_gemm(reset != 0);
+  return (int)v;
+}
 
 extern "C" const char *tsb_strerror(int status) {
   switch (status) {

@@ -1,0 +1,281 @@
+// Prefill 4-bit quantized matmul (M >= a few hundred rows): tcgen05 GEMM with
+// the weight dequantized into shared memory. B200 counterpart of the
+// reference's prefill_kernel (mlx-tree-spec src/mlx_tree_spec/qmm_packed.py:
+// 561-725), which dequantizes a BN x BK weight block into threadgroup memory
+// per K step (`T(float(q) * s + b)`, :635) and runs MLX's NAX tiles on it.
+//
+// CTA tile: 256 x-rows (two M=128 MMAs) by BN weight rows, K step 64 (= one
+// quantization group). Warp roles:
+//   warp 0     TMA producer: x tiles (two 128x64 bf16 boxes, 128-byte swizzle)
+//              and the packed codes of BN rows x 8 words per K step.
+//   warp 1     MMA issuer: 2 x 4 tcgen05.mma (M=128, N=BN, K=16) per K step
+//              into two TMEM accumulators (2*BN columns), commit frees the stage.
+//   warps 2-9  dequantizers: codes (shared) -> bf16 s*q + b -> the B tile in
+//              the K-major 128-byte-swizzle layout the MMA reads; then the
+//              epilogue: TMEM -> registers -> bf16 -> y.
+// Per stage the codes arrive with the x tile; the B tile of a stage is
+// rewritten only after the MMA that read it committed (the producer waits on
+// the stage's `empty` barrier before it refills the codes the dequantizers
+// wait on).
+//
+// Dequantization per packed word (8 codes): two masks and one shift split the
+// nibbles, three byte permutes place code | 0x4300 (= bf16 128 + q) in natural
+// order, an exact bf16 subtract of 128 gives q, and one bf16x2 fma rounds
+// s*q + b once to bf16 (the same value as bf16(fmaf(q, s, b)) whenever that
+// float32 sum is exact, i.e. for quantizer-produced weights).
+#include "sm100.cuh"
+
+namespace tsb {
+
+namespace {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 256;
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = 128 * BK * 2;  // one M half
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int C_BYTES = BN * 32;       // 8 words per row
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + B_BYTES + C_BYTES;
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int THREADS = 320;
+  static constexpr int DQ_THREADS = 256;
+  static constexpr int ROWS_PER_DQ = BN * 8 / DQ_THREADS;  // (row, word) items per dequant thread
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
+};
+
+TSB_HD uint32_t bf2_as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+TSB_HD __nv_bfloat162 u32_as_bf2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162 *>(&v); }
+
+// 8 codes of one word -> 4 bf16x2 (natural order) of s*q + b.
+TSB_HD void dequant_word(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2, uint32_t (&o)[4]) {
+  const uint32_t t0 = w & 0x0F0F0F0Fu;          // codes 0,2,4,6
+  const uint32_t t1 = (w >> 4) & 0x0F0F0F0Fu;   // codes 1,3,5,7
+  const uint32_t u0 = prmt(t0, t1, 0x5140u);    // bytes: q0 q1 q2 q3
+  const uint32_t u1 = prmt(t0, t1, 0x7362u);    // q4 q5 q6 q7
+  const uint32_t magic = 0x43434343u;
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+  const uint32_t v[4] = {prmt(u0, magic, 0x4140u), prmt(u0, magic, 0x4342u), prmt(u1, magic, 0x4140u),
+                         prmt(u1, magic, 0x4342u)};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 q = __hsub2(u32_as_bf2(v[i]), k128);
+    o[i] = bf2_as_u32(__hfma2(q, s2, b2));
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(320, 1)
+qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases,
+                uint16_t *__restrict__ y, int M, int N, int K, int ldy) {
+  using C = GemmCfg<BN>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t *full_x = bars;
+  uint64_t *full_c = bars + C::STAGES;
+  uint64_t *full_b = bars + 2 * C::STAGES;
+  uint64_t *empty = bars + 3 * C::STAGES;
+  uint64_t *acc_full = bars + 4 * C::STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4 * C::STAGES + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.x * C::BM;
+  const int n0 = blockIdx.y * BN;
+  const int G = K / 64;
+  const int num_k = G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_x[s], 1);
+      mbar_init(&full_c[s], 1);
+      mbar_init(&full_b[s], C::DQ_THREADS / 32);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto stage_ptr = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmap_x);
+      tma_prefetch_desc(&tmap_w);
+      int issued = 0;
+      for (int i = 0; i < num_k; ++i) {
+        const int s = i % C::STAGES;
+        if (i >= C::STAGES) {
+          if (!mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) break;
+        }
+        unsigned char *st = stage_ptr(s);
+        mbar_arrive_expect_tx(&full_x[s], 2 * C::A_BYTES);
+        tma_load_2d(st, &tmap_x, i * C::BK, m0, &full_x[s]);
+        tma_load_2d(st + C::A_BYTES, &tmap_x, i * C::BK, m0 + 128, &full_x[s]);
+        mbar_arrive_expect_tx(&full_c[s], C::C_BYTES);
+        tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &tmap_w, i * 8, n0, &full_c[s]);
+        issued = i + 1;
+      }
+      // drain: every issued load has landed before the CTA can exit
+      for (int i = (issued > C::STAGES ? issued - C::STAGES : 0); i < issued; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t par = (i / C::STAGES) & 1;
+        const unsigned long long t0 = globaltimer_ns();
+        while (!(mbar_try_wait(&full_x[s], par) && mbar_try_wait(&full_c[s], par))) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = idesc_bf16_f32(128, BN);
+    bool ok = true;
+    for (int i = 0; i < num_k && ok; ++i) {
+      const int s = i % C::STAGES;
+      const uint32_t par = (i / C::STAGES) & 1;
+      ok = warp_wait(&full_x[s], par) && warp_wait(&full_b[s], par);
+      if (!ok) break;
+      tc_fence_after();
+      if (elect_one()) {
+        unsigned char *st = stage_ptr(s);
+        const uint32_t a0 = smem_addr(st), a1 = smem_addr(st + C::A_BYTES), b = smem_addr(st + 2 * C::A_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          const uint64_t bd = desc_kmajor_sw128(b + kk * 32);
+          mma_ss_f16(tmem_base, desc_kmajor_sw128(a0 + kk * 32), bd, idesc, acc);
+          mma_ss_f16(tmem_base + BN, desc_kmajor_sw128(a1 + kk * 32), bd, idesc, acc);
+        }
+        mma_commit(&empty[s]);
+        if (i == num_k - 1) mma_commit(acc_full);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ---------------- dequantizers, then epilogue
+    const int t = threadIdx.x - 64;  // 0..255
+    const int j = t & 7;             // word within the group
+    const int rsub = t >> 3;         // 0..31
+    uint32_t sb_cur[C::ROWS_PER_DQ], sb_nxt[C::ROWS_PER_DQ];  // (s | b << 16)
+    auto load_sb = [&](int g, uint32_t (&dst)[C::ROWS_PER_DQ]) {
+#pragma unroll
+      for (int it = 0; it < C::ROWS_PER_DQ; ++it) {
+        const size_t idx = (size_t)(n0 + it * 32 + rsub) * G + g;
+        dst[it] = uint32_t(__ldg(scales + idx)) | (uint32_t(__ldg(biases + idx)) << 16);
+      }
+    };
+    load_sb(0, sb_cur);
+    bool ok = true;
+    for (int i = 0; i < num_k; ++i) {
+      const int s = i % C::STAGES;
+      const uint32_t par = (i / C::STAGES) & 1;
+      if (i + 1 < num_k) load_sb(i + 1, sb_nxt);
+      if (!warp_wait(&full_c[s], par)) { ok = false; break; }
+      unsigned char *st = stage_ptr(s);
+      const uint32_t *codes = reinterpret_cast<const uint32_t *>(st + 2 * C::A_BYTES + C::B_BYTES);
+      unsigned char *btile = st + 2 * C::A_BYTES;
+#pragma unroll
+      for (int it = 0; it < C::ROWS_PER_DQ; ++it) {
+        const int r = it * 32 + rsub;
+        const uint32_t w = codes[r * 8 + j];
+        const uint32_t sbv = sb_cur[it];
+        const __nv_bfloat162 s2 = u32_as_bf2((sbv & 0xFFFFu) | (sbv << 16));
+        const __nv_bfloat162 b2 = u32_as_bf2((sbv >> 16) | (sbv & 0xFFFF0000u));
+        uint32_t o[4];
+        dequant_word(w, s2, b2, o);
+        const uint32_t off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
+        *reinterpret_cast<uint4 *>(btile + off) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_b[s]);
+#pragma unroll
+      for (int it = 0; it < C::ROWS_PER_DQ; ++it) sb_cur[it] = sb_nxt[it];
+    }
+    // ---------------- epilogue
+    if (ok && warp_wait(acc_full, 0)) {
+      tc_fence_after();
+      const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+      const int half = (warp - 2) >> 2;       // which half of the columns
+      for (int mh = 0; mh < 2; ++mh) {
+        const int row = m0 + mh * 128 + q * 32 + lane;
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(mh * BN + c), r);
+          tmem_wait_ld();
+          if (row < M) {
+            uint32_t p[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p[e] = pack_bf16x2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+            uint4 *dst = reinterpret_cast<uint4 *>(y + (size_t)row * ldy + n0 + c);
+            dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+            dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int BN>
+int launch_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
+                int K, int ldy, cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  CUtensorMap tx, tw;
+  if (make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B) != TSB_OK)
+    return TSB_ECUDA;
+  if (make_tmap_2d(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)K / 8, (uint64_t)N, (uint64_t)K / 2, 8, BN,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) != TSB_OK)
+    return TSB_ECUDA;
+  static bool attr_set[2] = {false, false};
+  bool &done = attr_set[BN == 256 ? 1 : 0];
+  if (!done) {
+    if (cudaFuncSetAttribute(qmm_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) !=
+        cudaSuccess)
+      return TSB_ECUDA;
+    done = true;
+  }
+  dim3 grid((M + C::BM - 1) / C::BM, N / BN);
+  qmm_gemm_kernel<BN><<<grid, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, y, M, N, K, ldy);
+  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+}
+
+}  // namespace
+
+int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
+             int K, int ldy, cudaStream_t st) {
+  if (N % 256 == 0) return launch_gemm<256>(x, w, s, b, y, M, N, K, ldy, st);
+  return launch_gemm<128>(x, w, s, b, y, M, N, K, ldy, st);
+}
+
+unsigned int status_gemm(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+  if (reset && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_device_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace tsb

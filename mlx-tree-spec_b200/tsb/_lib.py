@@ -29,6 +29,7 @@ _P, _I, _Z, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_float
 SIGNATURES = {
     "tsb_strerror": (ctypes.c_char_p, [_I]),
     "tsb_version": (_I, []),
+    "tsb_device_status": (_I, [_P, _I]),
     "tsb_qmm_workspace_bytes": (_Z, [_I, _I, _I]),
     "tsb_qmm_w4g64": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "tsb_dequant_w4g64": (_I, [_P, _P, _P, _P, _I, _I, _P]),

@@ -120,3 +120,45 @@ def test_qmm_declines_and_rejects():
     assert tsb.quantized_matmul(x, w, s, s) is None  # N % 128: declined, caller falls back
     assert tsb.quantized_matmul(x, w, s, s, group_size=32) is None
     assert tsb.quantized_matmul(x.float(), w, s, s) is None
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 128), (300, 128, 192), (513, 384, 640), (1024, 512, 1024),
+                                   (257, 1024, 320)])
+def test_qmm_gemm_path_full_oracle(m, n, k):
+    """The tcgen05 GEMM path (M >= 256), odd M and N % 256 != 0 included."""
+    rng = np.random.default_rng(7000 + m + n + k)
+    x = gen.x_bf16(rng, m, k)
+    wq, s, b = gen.weights_w4g64(rng, n, k)
+    y = _run(x, wq, s, b)
+    ref = qmm.qmm(x, wq, s, b)
+    assert_close_rel(y, ref, REL, f"gemm {m}x{n}x{k}")
+    assert_close_rel(y, ref, REL_TIGHT, f"gemm {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("nk", [(34816, 5120), (5120, 17408), (6144, 5120)])
+def test_qmm_prefill_config3_sampled(nk):
+    """M = 4096; the oracle checks 48 x-rows x 256 weight rows."""
+    import tsb
+
+    n, k = nk
+    m = 4096
+    torch.manual_seed(3000 + n)
+    wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda") * 0.02)
+    rng = np.random.default_rng(3000 + n)
+    x = gen.x_bf16(rng, m, k)
+    y = tsb.quantized_matmul(dev_bf16(x), wq, s, b)
+    torch.cuda.synchronize()
+    rows = np.sort(rng.choice(m, size=48, replace=False))
+    cols = np.sort(rng.choice(n, size=256, replace=False))
+    ref = qmm.qmm(x[rows], wq[cols].cpu().numpy().view(np.uint32), host_bf16_bits(s[cols]), host_bf16_bits(b[cols]))
+    got = host_f32(y)[rows][:, cols]
+    assert_close_rel(got, ref, REL, f"prefill {nk}")
+    assert_close_rel(got, ref, REL_TIGHT, f"prefill {nk}")
+
+
+def test_device_status_clean_after_runs():
+    """No bounded device-side wait has given up during the tests."""
+    from tsb import _lib
+
+    lib = _lib.load()
+    assert lib.tsb_device_status(None, 0) == 0
