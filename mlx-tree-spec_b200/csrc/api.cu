@@ -49,6 +49,7 @@ int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, 
 }
 
 unsigned int status_gemm(bool reset);
+unsigned int status_ts(bool reset);
 
 }  // namespace tsb
 
@@ -57,8 +58,9 @@ unsigned int status_gemm(bool reset);
 // out (TSB_ETIMEOUT). reset != 0 clears the record.
 extern "C" int tsb_device_status(tsb_stream_t stream, int reset) {
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return TSB_ECUDA;
-  const unsigned int v = tsb::status_gemm(reset != 0);
-  return (int)v;
+  const unsigned int a = tsb::status_gemm(reset != 0);
+  const unsigned int b = tsb::status_ts(reset != 0);
+  return (int)(a ? a : b);
 }
 
 extern "C" const char *tsb_strerror(int status) {

@@ -75,4 +75,45 @@ TSB_HD uint4 ldg_nc_v4(const void *p) {
   return r;
 }
 
+TSB_HD uint32_t bf2_as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
+TSB_HD __nv_bfloat162 u32_as_bf2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162 *>(&v); }
+
+// 8 codes of one MLX word -> 4 bf16x2 (natural order) of s*q + b. Two masks
+// and a shift split the nibbles, byte permutes place (code | 0x4300) = bf16
+// 128 + q, an exact bf16 subtract of 128 leaves q, and one bf16x2 fma rounds
+// s*q + b once to bf16 (equal to bf16(fmaf(q, s, b)) whenever that float32
+// sum is exact, as it is for quantizer-produced (s, b)).
+TSB_HD void dequant_word(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2, uint32_t (&o)[4]) {
+  const uint32_t t0 = w & 0x0F0F0F0Fu;          // codes 0,2,4,6
+  const uint32_t t1 = (w >> 4) & 0x0F0F0F0Fu;   // codes 1,3,5,7
+  const uint32_t u0 = prmt(t0, t1, 0x5140u);    // bytes: q0 q1 q2 q3
+  const uint32_t u1 = prmt(t0, t1, 0x7362u);    // q4 q5 q6 q7
+  const uint32_t magic = 0x43434343u;
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
+  const uint32_t v[4] = {prmt(u0, magic, 0x4140u), prmt(u0, magic, 0x4342u), prmt(u1, magic, 0x4140u),
+                         prmt(u1, magic, 0x4342u)};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 q = __hsub2(u32_as_bf2(v[i]), k128);
+    o[i] = bf2_as_u32(__hfma2(q, s2, b2));
+  }
+}
+
+// 8 codes of one MLX word -> 4 bf16x2 (natural order) of bf16(s*q), without
+// the bias: (code | 0x4300) is bf16 128 + q, and fma(128 + q, s, -128 s) =
+// s*q rounded once (s and -128 s are exact bf16). The bias enters the matmul
+// separately (sum_k b x_k per group), so the per-element work is one fma per
+// pair after the byte shuffles.
+TSB_HD void dequant_word_scaled(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 ns2, uint32_t (&o)[4]) {
+  const uint32_t t0 = w & 0x0F0F0F0Fu;
+  const uint32_t t1 = (w >> 4) & 0x0F0F0F0Fu;
+  const uint32_t u0 = prmt(t0, t1, 0x5140u);
+  const uint32_t u1 = prmt(t0, t1, 0x7362u);
+  const uint32_t magic = 0x43434343u;
+  const uint32_t v[4] = {prmt(u0, magic, 0x4140u), prmt(u0, magic, 0x4342u), prmt(u1, magic, 0x4140u),
+                         prmt(u1, magic, 0x4342u)};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = bf2_as_u32(__hfma2(u32_as_bf2(v[i]), s2, ns2));
+}
+
 }  // namespace tsb

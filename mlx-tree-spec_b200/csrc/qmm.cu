@@ -4,24 +4,24 @@
 #include "common.cuh"
 
 namespace tsb {
-size_t qmm_small_workspace_bytes(int M, int K);
-int qmm_small(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M,
-              int N, int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st);
+int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
+           int K, int ldy, cudaStream_t st);
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
              int K, int ldy, cudaStream_t st);
 
-// Rows from which the tcgen05 GEMM (dequantize into shared memory, 256-row
-// tiles) takes over from the small-M kernel.
-constexpr int kGemmMinRows = 256;
+// Rows above which the tcgen05 GEMM (dequantize into shared memory, 256-row
+// tiles) takes over from the verify-pass kernel (weights dequantized into
+// TMEM, tokens as the MMA's N <= 128).
+constexpr int kTsMaxRows = 128;
 }  // namespace tsb
 
 using namespace tsb;
 
 extern "C" size_t tsb_qmm_workspace_bytes(int M, int N, int K) {
   (void)N;
-  if (M <= 0 || K <= 0) return 0;
-  if (M >= kGemmMinRows) return 0;
-  return qmm_small_workspace_bytes(M, K);
+  (void)M;
+  (void)K;
+  return 0;  // neither path needs scratch memory
 }
 
 extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const void *biases, void *y,
@@ -31,10 +31,11 @@ extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scale
   if (K % 64 || N % 128) return TSB_EUNSUPPORTED;
   if (ldy % 8) return TSB_EINVAL;
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16)) return TSB_EINVAL;
-  if (M >= kGemmMinRows)
-    return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
-                    ldy, (cudaStream_t)stream);
-  if (!ws || !aligned(ws, 16)) return TSB_EINVAL;
-  return qmm_small((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M,
-                   N, K, ldy, ws, ws_bytes, (cudaStream_t)stream);
+  (void)ws;
+  (void)ws_bytes;
+  if (M <= kTsMaxRows)
+    return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
+                  ldy, (cudaStream_t)stream);
+  return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
+                  ldy, (cudaStream_t)stream);
 }

@@ -45,26 +45,6 @@ struct GemmCfg {
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
 };
 
-TSB_HD uint32_t bf2_as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t *>(&v); }
-TSB_HD __nv_bfloat162 u32_as_bf2(uint32_t v) { return *reinterpret_cast<__nv_bfloat162 *>(&v); }
-
-// 8 codes of one word -> 4 bf16x2 (natural order) of s*q + b.
-TSB_HD void dequant_word(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2, uint32_t (&o)[4]) {
-  const uint32_t t0 = w & 0x0F0F0F0Fu;          // codes 0,2,4,6
-  const uint32_t t1 = (w >> 4) & 0x0F0F0F0Fu;   // codes 1,3,5,7
-  const uint32_t u0 = prmt(t0, t1, 0x5140u);    // bytes: q0 q1 q2 q3
-  const uint32_t u1 = prmt(t0, t1, 0x7362u);    // q4 q5 q6 q7
-  const uint32_t magic = 0x43434343u;
-  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.f, 128.f);
-  const uint32_t v[4] = {prmt(u0, magic, 0x4140u), prmt(u0, magic, 0x4342u), prmt(u1, magic, 0x4140u),
-                         prmt(u1, magic, 0x4342u)};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 q = __hsub2(u32_as_bf2(v[i]), k128);
-    o[i] = bf2_as_u32(__hfma2(q, s2, b2));
-  }
-}
-
 template <int BN>
 __global__ void __launch_bounds__(320, 1)
 qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
