@@ -139,6 +139,25 @@ int tsb_tree_attn(const void *q,
                   int B, int T, int Hq, int Hkv, int D, int n_kv, int tail, int kv_capacity,
                   float scale, void *out, float *lse, void *ws, size_t ws_bytes, tsb_stream_t stream);
 
+/* Allocation-free tsb_tree_attn, for callers that cannot pass a workspace
+ * (a host whose device memory belongs to a pool allocator it cannot call from
+ * the decode loop, an FFI binding without a device allocator, a serving loop
+ * that forbids allocation). Same arguments and result as tsb_tree_attn minus
+ * (ws, ws_bytes). The split-KV scratch is a fixed 16 MiB array inside the
+ * library, reserved on each GPU that loads it and held until the process
+ * exits; a call whose tsb_tree_attn_workspace_bytes() exceeds 16 MiB returns
+ * TSB_EWORKSPACE without launching anything (use tsb_tree_attn with a
+ * workspace then). The first call on each device looks up the array's device
+ * address: make it before any stream capture. All calls on a device share the
+ * array, so calls whose GPU work overlaps race: serialize them. No counterpart
+ * in the reference (its MLX kernels allocate their outputs per call). */
+int tsb_tree_attn_noalloc(const void *q,
+                          const void *k, const void *k_scales, const void *k_biases,
+                          const void *v, const void *v_scales, const void *v_biases,
+                          int kv_format, const int32_t *parents, const uint64_t *bits,
+                          int B, int T, int Hq, int Hkv, int D, int n_kv, int tail, int kv_capacity,
+                          float scale, void *out, float *lse, tsb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

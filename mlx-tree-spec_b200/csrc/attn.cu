@@ -24,6 +24,8 @@
 // MLX_Q8_G64 rows are dequantized (s * q + b, rounded to bf16) into the tile.
 #include "common.cuh"
 
+#include <mutex>
+
 namespace tsb {
 
 namespace {
@@ -531,4 +533,63 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
     if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
   }
   return TSB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of tsb_tree_attn.
+//
+// Some callers cannot hand this library a workspace: a host whose device
+// memory is owned by a pool allocator it cannot call into from the decode
+// loop, a language binding (cgo, JNI, N-API) that has no device allocator of
+// its own, or a serving loop that forbids any allocation once it is running.
+// For them the split-KV partials live in a fixed array in the library's own
+// device memory, reserved when the library is loaded on a device and held
+// until the process exits (kAttnScratchBytes = 16 MiB per GPU). The first call
+// on each device looks up that array's device address; make that first call
+// before capturing a stream into a graph.
+//
+// The array is shared by every call on a device and keeps the last call's
+// contents. Nothing in it must start at zero: each call's first kernel writes
+// every partial that its combine kernel then reads. Calls whose GPU work can
+// overlap (different streams, or graphs launched concurrently) race on it and
+// must be serialized by the caller.
+namespace tsb {
+namespace {
+
+constexpr size_t kAttnScratchBytes = 16u << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_attn_scratch[kAttnScratchBytes];
+
+// Device address of g_attn_scratch on the current device. The host-side name
+// of a __device__ array is only a stand-in, never a device address, so it is
+// looked up once per device with cudaGetSymbolAddress (with that device
+// current) and cached. nullptr if the lookup fails.
+void *attn_scratch_ptr() {
+  static std::mutex mu;
+  static void *ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_attn_scratch) != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace
+}  // namespace tsb
+
+extern "C" int tsb_tree_attn_noalloc(const void *q, const void *k, const void *k_scales, const void *k_biases,
+                                     const void *v, const void *v_scales, const void *v_biases, int kv_format,
+                                     const int32_t *parents, const uint64_t *bits, int B, int T, int Hq, int Hkv,
+                                     int D, int n_kv, int tail, int kv_capacity, float scale, void *out, float *lse,
+                                     tsb_stream_t stream) {
+  if (B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || n_kv <= 0) return TSB_EINVAL;
+  const size_t need = tsb_tree_attn_workspace_bytes(B, T, Hq, Hkv, D, n_kv, kv_format);
+  if (need > tsb::kAttnScratchBytes) return TSB_EWORKSPACE;  // beyond the fixed scratch: use tsb_tree_attn
+  void *scratch = tsb::attn_scratch_ptr();
+  if (!scratch) return TSB_ECUDA;
+  return tsb_tree_attn(q, k, k_scales, k_biases, v, v_scales, v_biases, kv_format, parents, bits, B, T, Hq, Hkv, D,
+                       n_kv, tail, kv_capacity, scale, out, lse, scratch, tsb::kAttnScratchBytes, stream);
 }

@@ -37,6 +37,8 @@ SIGNATURES = {
     "tsb_tree_attn_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     "tsb_tree_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
                            _P, _P, _P, _Z, _P]),
+    "tsb_tree_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
+                                   _P, _P, _P]),
 }
 
 
