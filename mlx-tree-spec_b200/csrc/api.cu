@@ -50,6 +50,7 @@ int make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, 
 
 unsigned int status_gemm(bool reset);
 unsigned int status_ts(bool reset);
+unsigned int status_attn_tc(bool reset);
 
 }  // namespace tsb
 
@@ -60,7 +61,8 @@ extern "C" int tsb_device_status(tsb_stream_t stream, int reset) {
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return TSB_ECUDA;
   const unsigned int a = tsb::status_gemm(reset != 0);
   const unsigned int b = tsb::status_ts(reset != 0);
-  return (int)(a ? a : b);
+  const unsigned int c = tsb::status_attn_tc(reset != 0);
+  return (int)(a ? a : (b ? b : c));
 }
 
 extern "C" const char *tsb_strerror(int status) {

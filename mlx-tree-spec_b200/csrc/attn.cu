@@ -447,18 +447,33 @@ size_t attn_smem_bytes() {
 
 }  // namespace
 
+void plan_attn_tc(int B, int T, int Hq, int Hkv, int n_kv, int &row_blocks, int &splits, int &tiles_per_split);
+int launch_attn_tc(const uint16_t *q, const uint16_t *k, const uint16_t *v, const int32_t *parents,
+                   const unsigned long long *bits, int B, int T, int Hq, int Hkv, int n_kv, int tail, int cap,
+                   float scale, uint16_t *out, float *lse, float *part_o, float *part_ml, cudaStream_t st);
+
 }  // namespace tsb
 
 using namespace tsb;
 
+// Key splits of a call: the tcgen05 kernel for bf16 KV, the warp-MMA kernel
+// (8-bit formats, dequantized while staged) otherwise.
+static int attn_splits(int B, int T, int Hq, int Hkv, int n_kv, int kv_format) {
+  if (kv_format == TSB_KV_BF16) {
+    int rb, splits, tps;
+    plan_attn_tc(B, T, Hq, Hkv, n_kv, rb, splits, tps);
+    return splits;
+  }
+  return plan_attn(B, T, Hq, Hkv, n_kv).splits;
+}
+
 extern "C" size_t tsb_tree_attn_workspace_bytes(int B, int T, int Hq, int Hkv, int D, int n_kv, int kv_format) {
   (void)D;
-  (void)kv_format;
   if (B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || n_kv <= 0) return 0;
-  const AttnPlan p = plan_attn(B, T, Hq, Hkv, n_kv);
-  if (p.splits <= 1) return 0;
+  const int splits = attn_splits(B, T, Hq, Hkv, n_kv, kv_format);
+  if (splits <= 1) return 0;
   const size_t rows = (size_t)B * Hq * T;
-  return (size_t)p.splits * rows * (AT_D + 2) * sizeof(float) + 256;
+  return (size_t)splits * rows * (AT_D + 2) * sizeof(float) + 256;
 }
 
 extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales, const void *k_biases,
@@ -479,6 +494,29 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
   if (kv_format < 0 || kv_format > 2) return TSB_EUNSUPPORTED;
   if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16)) return TSB_EINVAL;
 
+  const size_t rows = (size_t)B * Hq * T;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (kv_format == TSB_KV_BF16) {
+    const int splits = attn_splits(B, T, Hq, Hkv, n_kv, kv_format);
+    float *part_o = nullptr, *part_ml = nullptr;
+    if (splits > 1) {
+      const size_t need = tsb_tree_attn_workspace_bytes(B, T, Hq, Hkv, D, n_kv, kv_format);
+      if (!ws || ws_bytes < need) return TSB_EWORKSPACE;
+      if (!aligned(ws, 16)) return TSB_EINVAL;
+      part_o = (float *)ws;
+      part_ml = part_o + (size_t)splits * rows * AT_D;
+    }
+    int r = launch_attn_tc((const uint16_t *)q, (const uint16_t *)k, (const uint16_t *)v, parents,
+                           (const unsigned long long *)bits, B, T, Hq, Hkv, n_kv, tail, kv_capacity, scale,
+                           (uint16_t *)out, lse, part_o, part_ml, st);
+    if (r != TSB_OK) return r;
+    if (splits > 1) {
+      tree_attn_combine_kernel<<<(unsigned)rows, AT_D, 0, st>>>(part_o, part_ml, splits, (int)rows,
+                                                              (uint16_t *)out, lse);
+      if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
+    }
+    return TSB_OK;
+  }
   const AttnPlan p = plan_attn(B, T, Hq, Hkv, n_kv);
   AttnArgs a;
   a.q = (const uint16_t *)q;
@@ -496,7 +534,6 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
   a.lse = lse;
   a.part_o = nullptr;
   a.part_ml = nullptr;
-  const size_t rows = (size_t)B * Hq * T;
   if (p.splits > 1) {
     const size_t need = tsb_tree_attn_workspace_bytes(B, T, Hq, Hkv, D, n_kv, kv_format);
     if (!ws || ws_bytes < need) return TSB_EWORKSPACE;
@@ -507,7 +544,6 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
   const size_t smem = attn_smem_bytes();
   const dim3 grid(B * Hkv * p.row_blocks, p.splits);
   const dim3 block(p.rows_per_cta * 2);  // 32 threads per 16 rows
-  cudaStream_t st = (cudaStream_t)stream;
   cudaError_t e;
   switch (kv_format) {
     case TSB_KV_BF16:

@@ -1,0 +1,453 @@
+// Tree-mask flash attention on tcgen05 (bf16 KV). Same contract as the
+// reference's tree_flash (mlx-tree-spec src/mlx_tree_spec/tree_flash.py:
+// 151-196; visibility at 40-45) and the same split-KV partial format and
+// combine kernel as attn.cu.
+//
+// CTA = (request b, KV head, block of 128 packed query rows, key split). The
+// G*T query rows of a KV head (row = head_local * T + node) are contiguous in
+// q [B, Hq, T, D], so one 2D TMA box brings them; rows past the KV head's G*T
+// are computed and dropped.
+//   warp 0     TMA: Q once (four 64-wide D boxes, 128-byte swizzle), then K and
+//              V tiles of 64 keys through two rings.
+//   warp 1     MMA: S_j = Q K_j^T (tcgen05.mma, A = Q and B = K from shared
+//              memory, K-major, M=128, N=64, K=256) into one of two TMEM score
+//              buffers; O += P_j V_j with P_j from TMEM and V_j from shared
+//              memory as an MN-major operand (M=128, N=256, K=64). S_{j+1} is
+//              issued before O += P_j V_j so scores overlap the softmax.
+//   warps 2-5  softmax, one thread per query row (= TMEM lane): scores ->
+//              scale, ancestor mask, online max/sum in the exp2 domain -> P as
+//              bf16 into TMEM. O is rescaled in TMEM only when the running max
+//              grows by more than 2^8 (values stay bounded in between), after
+//              the previous P V has completed. Epilogue: O / l -> bf16 out, or
+//              normalised partials plus (max, sum) for the combine kernel.
+// TMEM (512 columns): O [0, 256), S0 [256, 320), S1 [320, 384), P0 [384, 416),
+// P1 [416, 448).
+#include "sm100.cuh"
+
+namespace tsb {
+
+namespace {
+
+constexpr int TC_KT = 64;                       // keys per tile
+constexpr int TC_D = 256;
+constexpr int TC_QBOX = 128 * 128;              // one 64-wide D box of 128 rows (bytes)
+constexpr int TC_KVBOX = TC_KT * 128;           // one 64-wide D box of 64 keys
+constexpr int TC_Q_BYTES = 4 * TC_QBOX;         // 64 KB
+constexpr int TC_KV_BYTES = 4 * TC_KVBOX;       // 32 KB per K or V tile
+constexpr int TC_NK = 2, TC_NV = 2;
+constexpr int TC_THREADS = 192;
+constexpr size_t TC_SMEM = TC_Q_BYTES + (TC_NK + TC_NV) * TC_KV_BYTES + 1024 + 1024;
+constexpr uint32_t TC_O = 0, TC_S0 = 256, TC_P0 = 384;
+constexpr float TC_RESCALE_LOG2 = 8.f;
+
+struct TcArgs {
+  const int32_t *parents;
+  const unsigned long long *bits;
+  int B, T, Hq, Hkv, n_kv, tail, cap;
+  int row_blocks, splits, tiles_per_split;
+  float scale_log2;
+  uint16_t *out;
+  float *lse;
+  float *part_o;
+  float *part_ml;
+};
+
+TSB_HD float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// MN-major operand, 128-byte swizzle: 64-element rows of 128 B along MN, 8-row
+// K groups 1024 B apart (SBO), 64-element MN blocks `lbo` bytes apart (LBO).
+TSB_HD uint64_t desc_mnmajor_sw128(uint32_t smem_byte_addr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_byte_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                    const __grid_constant__ CUtensorMap tmap_v, TcArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *sQ = smem;
+  unsigned char *sK = sQ + TC_Q_BYTES;
+  unsigned char *sV = sK + TC_NK * TC_KV_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sV + TC_NV * TC_KV_BYTES);
+  uint64_t *q_full = bars;
+  uint64_t *k_full = bars + 1, *k_free = k_full + TC_NK;
+  uint64_t *v_full = k_free + TC_NK, *v_free = v_full + TC_NV;
+  uint64_t *s_full = v_free + TC_NV, *s_free = s_full + 2;
+  uint64_t *p_full = s_free + 2, *p_free = p_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(p_free + 2);
+  unsigned long long *sBits = reinterpret_cast<unsigned long long *>(tmem_slot + 2);  // [T <= 64]
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int G = a.Hq / a.Hkv;
+  const int R = G * a.T;
+  int unit = blockIdx.x;
+  const int split = blockIdx.y;
+  const int rb = unit % a.row_blocks;
+  unit /= a.row_blocks;
+  const int kh = unit % a.Hkv;
+  const int b = unit / a.Hkv;
+  const int n_tiles_total = (a.n_kv + TC_KT - 1) / TC_KT;
+  const int j_begin = split * a.tiles_per_split;
+  const int j_end = min(n_tiles_total, j_begin + a.tiles_per_split);
+  const int nt = j_end - j_begin;
+  const int tail_lo = a.n_kv - a.tail;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < TC_NK; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_free[i], 1); }
+    for (int i = 0; i < TC_NV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_free[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+    }
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  // node masks, from the parent array or given
+  for (int node = threadIdx.x; node < a.T; node += blockDim.x) {
+    unsigned long long m = 0;
+    if (a.parents) {
+      const int32_t *p = a.parents + (size_t)b * a.T;
+      int j = node;
+      bool ok = true;
+      for (int steps = 0; steps <= a.T && j != -1; ++steps) {
+        m |= 1ull << j;
+        const int pj = p[j];
+        if (!(pj == -1 || (pj >= 0 && pj < j))) { ok = false; break; }
+        j = pj;
+      }
+      if (!ok) m = 0;
+    } else {
+      m = a.bits[(size_t)b * a.T + node];
+    }
+    sBits[node] = m;
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const size_t kv_row0 = ((size_t)b * a.Hkv + kh) * (size_t)a.cap;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (elect_one()) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      const int qrow = ((b * a.Hq + kh * G) * a.T) + rb * 128;
+      mbar_arrive_expect_tx(q_full, TC_Q_BYTES);
+#pragma unroll
+      for (int d = 0; d < 4; ++d) tma_load_2d(sQ + d * TC_QBOX, &tmap_q, d * 64, qrow, q_full);
+      int ik = 0, iv = 0;
+      bool ok = true;
+      // K runs up to two tiles ahead of V (the MMA needs K_{j+1} before V_j)
+      for (int j = 0; j < nt && ok; ++j) {
+        const int key0 = (int)kv_row0 + (j_begin + j) * TC_KT;
+        {
+          const int s = ik % TC_NK;
+          if (ik >= TC_NK && !mbar_wait(&k_free[s], ((ik / TC_NK) - 1) & 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[s], TC_KV_BYTES);
+#pragma unroll
+          for (int d = 0; d < 4; ++d)
+            tma_load_2d(sK + s * TC_KV_BYTES + d * TC_KVBOX, &tmap_k, d * 64, key0, &k_full[s]);
+          ++ik;
+        }
+        {
+          const int s = iv % TC_NV;
+          if (iv >= TC_NV && !mbar_wait(&v_free[s], ((iv / TC_NV) - 1) & 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[s], TC_KV_BYTES);
+#pragma unroll
+          for (int d = 0; d < 4; ++d)
+            tma_load_2d(sV + s * TC_KV_BYTES + d * TC_KVBOX, &tmap_v, d * 64, key0, &v_full[s]);
+          ++iv;
+        }
+      }
+      // drain: the issued loads have landed before the CTA can exit
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(q_full, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
+      }
+      for (int i = (ik > TC_NK ? ik - TC_NK : 0); i < ik; ++i) {
+        const unsigned long long t1 = globaltimer_ns();
+        while (!mbar_try_wait(&k_full[i % TC_NK], (i / TC_NK) & 1)) {
+          if (globaltimer_ns() - t1 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
+        }
+      }
+      for (int i = (iv > TC_NV ? iv - TC_NV : 0); i < iv; ++i) {
+        const unsigned long long t1 = globaltimer_ns();
+        while (!mbar_try_wait(&v_full[i % TC_NV], (i / TC_NV) & 1)) {
+          if (globaltimer_ns() - t1 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    const uint32_t idesc_s = idesc_bf16_f32(128, TC_KT);
+    const uint32_t idesc_o = idesc_bf16_f32(128, TC_D) | (1u << 16);  // B (V) MN-major
+    bool ok = warp_wait(q_full, 0);
+    auto issue_s = [&](int j) -> bool {
+      const int s = j % TC_NK, sb = j & 1;
+      if (!warp_wait(&k_full[s], (j / TC_NK) & 1)) return false;
+      if (j >= 2 && !warp_wait(&s_free[sb], ((j >> 1) - 1) & 1)) return false;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t qa = smem_addr(sQ), kb = smem_addr(sK + s * TC_KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) {
+          const uint32_t off_q = (kk >> 2) * TC_QBOX + (kk & 3) * 32;
+          const uint32_t off_k = (kk >> 2) * TC_KVBOX + (kk & 3) * 32;
+          mma_ss_f16(tmem + TC_S0 + sb * 64, desc_kmajor_sw128(qa + off_q), desc_kmajor_sw128(kb + off_k), idesc_s,
+                     kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[sb]);
+        mma_commit(&k_free[s]);
+      }
+      __syncwarp();
+      return true;
+    };
+    auto issue_pv = [&](int j) -> bool {
+      const int s = j % TC_NV, pb = j & 1;
+      if (!warp_wait(&v_full[s], (j / TC_NV) & 1)) return false;
+      if (!warp_wait(&p_full[pb], (j >> 1) & 1)) return false;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t vb = smem_addr(sV + s * TC_KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TC_KT / 16; ++kk) {
+          mma_ts_f16(tmem + TC_O, tmem + TC_P0 + pb * 32 + kk * 8, desc_mnmajor_sw128(vb + kk * 2048, TC_KVBOX),
+                     idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&v_free[s]);
+        mma_commit(&p_free[pb]);  // completes after this and every earlier MMA
+      }
+      __syncwarp();
+      return true;
+    };
+    if (ok && nt > 0) ok = issue_s(0);
+    for (int j = 0; j < nt && ok; ++j) {
+      if (j + 1 < nt) ok = issue_s(j + 1);
+      if (ok) ok = issue_pv(j);
+    }
+  } else {
+    // ---------------- softmax / epilogue (thread = query row = TMEM lane)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int gr = rb * 128 + r;
+    const bool row_valid = gr < R;
+    const int node = row_valid ? gr % a.T : 0;
+    const unsigned long long mybits = sBits[node];
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    float m = -INFINITY, l = 0.f;  // running max (log2 domain) and sum
+    bool ok = true;
+    for (int j = 0; j < nt && ok; ++j) {
+      const int sb = j & 1;
+      ok = warp_wait(&s_full[sb], (j >> 1) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[64];
+      {
+        uint32_t (&lo)[32] = *reinterpret_cast<uint32_t (*)[32]>(&sr[0]);
+        uint32_t (&hi)[32] = *reinterpret_cast<uint32_t (*)[32]>(&sr[32]);
+        tmem_ld32(lane_base + TC_S0 + sb * 64, lo);
+        tmem_ld32(lane_base + TC_S0 + sb * 64 + 32, hi);
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      // scale + mask
+      const int key0 = (j_begin + j) * TC_KT;
+      const bool need_mask = (key0 + TC_KT > tail_lo) || (key0 + TC_KT > a.n_kv);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        float v = __uint_as_float(sr[e]) * a.scale_log2;
+        if (need_mask) {
+          const int key = key0 + e;
+          bool vis = key < a.n_kv;
+          if (vis && key >= tail_lo) vis = (mybits >> (key - tail_lo)) & 1ull;
+          if (!vis) v = -INFINITY;
+        }
+        sr[e] = __float_as_uint(v);
+        tmax = fmaxf(tmax, v);
+      }
+      // P V_{j-2} must be done before P_j reuses its buffer; waiting here also
+      // keeps every p_free wait below at most one phase behind.
+      if (j >= 2) {
+        ok = warp_wait(&p_free[sb], ((j >> 1) - 1) & 1);
+        if (!ok) break;
+      }
+      // lazy rescale: move the reference max only when it grows by > 2^8
+      const bool grow = tmax > m + TC_RESCALE_LOG2;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = grow ? tmax : m;
+        const float alpha = (m == -INFINITY) ? 0.f : ex2(m - m_new);
+        if (j > 0) {  // O holds earlier tiles: wait for P V_{j-1} (and all before), then scale O in place
+          ok = warp_wait(&p_free[sb ^ 1], ((j - 1) >> 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < TC_D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + TC_O + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(lane_base + TC_O + c, o);
+          }
+          tmem_wait_st();
+        }
+        l *= alpha;
+        m = m_new;
+      }
+      const float base = (m == -INFINITY) ? 0.f : m;
+      uint32_t pk[32];
+      float psum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float p0 = ex2(__uint_as_float(sr[2 * e]) - base);
+        const float p1 = ex2(__uint_as_float(sr[2 * e + 1]) - base);
+        psum += p0 + p1;
+        pk[e] = pack_bf16x2(p0, p1);
+      }
+      l += psum;
+      // P_j into TMEM (its buffer was released above)
+      tc_fence_after();
+      tmem_st32(lane_base + TC_P0 + sb * 32, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+    }
+    // ---------------- epilogue
+    if (ok && nt > 0 && warp_wait(&p_free[(nt - 1) & 1], ((nt - 1) >> 1) & 1)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int hl = gr / a.T;
+      const size_t orow = ((size_t)b * a.Hq + (size_t)kh * G + hl) * a.T + node;
+#pragma unroll 1
+      for (int c = 0; c < TC_D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(lane_base + TC_O + c, o);
+        tmem_wait_ld();
+        if (!row_valid) continue;
+        if (a.splits == 1) {
+          uint32_t pkd[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            pkd[e] = pack_bf16x2(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+          uint4 *dst = reinterpret_cast<uint4 *>(a.out + orow * TC_D + c);
+          dst[0] = make_uint4(pkd[0], pkd[1], pkd[2], pkd[3]);
+          dst[1] = make_uint4(pkd[4], pkd[5], pkd[6], pkd[7]);
+          dst[2] = make_uint4(pkd[8], pkd[9], pkd[10], pkd[11]);
+          dst[3] = make_uint4(pkd[12], pkd[13], pkd[14], pkd[15]);
+        } else {
+          const size_t prow = (size_t)split * a.B * a.Hq * a.T + orow;
+          float4 *dst = reinterpret_cast<float4 *>(a.part_o + prow * TC_D + c);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            dst[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                                 __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+        }
+      }
+      if (row_valid) {
+        if (a.splits == 1) {
+          if (a.lse) a.lse[orow] = l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+        } else {
+          const size_t prow = (size_t)split * a.B * a.Hq * a.T + orow;
+          a.part_ml[prow * 2 + 0] = m;
+          a.part_ml[prow * 2 + 1] = l;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+// Plan of the tcgen05 path: row blocks of 128 packed query rows, tiles of 64
+// keys, splits so that the grid covers the SMs about once.
+void plan_attn_tc(int B, int T, int Hq, int Hkv, int n_kv, int &row_blocks, int &splits, int &tiles_per_split) {
+  const int R = (Hq / Hkv) * T;
+  row_blocks = (R + 127) / 128;
+  const int units = B * Hkv * row_blocks;
+  const int n_tiles = (n_kv + TC_KT - 1) / TC_KT;
+  int s = sm_count() / units;  // one CTA per SM (TMEM 512 columns): stay within one wave
+  if (s > n_tiles / 4) s = n_tiles / 4;
+  if (s < 1) s = 1;
+  tiles_per_split = (n_tiles + s - 1) / s;
+  splits = (n_tiles + tiles_per_split - 1) / tiles_per_split;
+}
+
+int launch_attn_tc(const uint16_t *q, const uint16_t *k, const uint16_t *v, const int32_t *parents,
+                   const unsigned long long *bits, int B, int T, int Hq, int Hkv, int n_kv, int tail, int cap,
+                   float scale, uint16_t *out, float *lse, float *part_o, float *part_ml, cudaStream_t st) {
+  TcArgs a;
+  a.parents = parents;
+  a.bits = bits;
+  a.B = B; a.T = T; a.Hq = Hq; a.Hkv = Hkv; a.n_kv = n_kv; a.tail = tail; a.cap = cap;
+  plan_attn_tc(B, T, Hq, Hkv, n_kv, a.row_blocks, a.splits, a.tiles_per_split);
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = out;
+  a.lse = lse;
+  a.part_o = part_o;
+  a.part_ml = part_ml;
+  CUtensorMap tq, tk, tv;
+  if (make_tmap_2d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, TC_D, (uint64_t)B * Hq * T, TC_D * 2, 64, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B) != TSB_OK)
+    return TSB_ECUDA;
+  if (make_tmap_2d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, TC_D, (uint64_t)B * Hkv * cap, TC_D * 2, 64, TC_KT,
+                   CU_TENSOR_MAP_SWIZZLE_128B) != TSB_OK)
+    return TSB_ECUDA;
+  if (make_tmap_2d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, TC_D, (uint64_t)B * Hkv * cap, TC_D * 2, 64, TC_KT,
+                   CU_TENSOR_MAP_SWIZZLE_128B) != TSB_OK)
+    return TSB_ECUDA;
+  static int attr_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (attr_dev != dev) {
+    if (cudaFuncSetAttribute(tree_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM) !=
+        cudaSuccess)
+      return TSB_ECUDA;
+    attr_dev = dev;
+  }
+  const dim3 grid(B * Hkv * a.row_blocks, a.splits);
+  tree_attn_tc_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(tq, tk, tv, a);
+  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+}
+
+unsigned int status_attn_tc(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+  if (reset && v) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_device_status, &z, sizeof(z));
+  }
+  return v;
+}
+
+}  // namespace tsb
