@@ -497,6 +497,7 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
   const size_t rows = (size_t)B * Hq * T;
   cudaStream_t st = (cudaStream_t)stream;
   if (kv_format == TSB_KV_BF16) {
+    if (!(scale > 0.f)) return TSB_EUNSUPPORTED;  // the kernel takes row maxima of unscaled scores
     const int splits = attn_splits(B, T, Hq, Hkv, n_kv, kv_format);
     float *part_o = nullptr, *part_ml = nullptr;
     if (splits > 1) {

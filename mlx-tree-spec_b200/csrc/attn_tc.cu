@@ -254,6 +254,8 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     const int node = row_valid ? gr % a.T : 0;
     const unsigned long long mybits = sBits[node];
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const float sl2 = a.scale_log2;
+    const int n_kv = a.n_kv;
     float m = -INFINITY, l = 0.f;  // running max (log2 domain) and sum
     bool ok = true;
     for (int j = 0; j < nt && ok; ++j) {
@@ -272,22 +274,26 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
-      // scale + mask
+      // mask (only the tail and the last tile need it), then the tile max of the
+      // raw scores in eight independent chains; the scale is applied in the exp
       const int key0 = (j_begin + j) * TC_KT;
-      const bool need_mask = (key0 + TC_KT > tail_lo) || (key0 + TC_KT > a.n_kv);
-      float tmax = -INFINITY;
+      if ((key0 + TC_KT > tail_lo) || (key0 + TC_KT > n_kv)) {
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        float v = __uint_as_float(sr[e]) * a.scale_log2;
-        if (need_mask) {
+        for (int e = 0; e < 64; ++e) {
           const int key = key0 + e;
-          bool vis = key < a.n_kv;
+          bool vis = key < n_kv;
           if (vis && key >= tail_lo) vis = (mybits >> (key - tail_lo)) & 1ull;
-          if (!vis) v = -INFINITY;
+          if (!vis) sr[e] = __float_as_uint(-INFINITY);
         }
-        sr[e] = __float_as_uint(v);
-        tmax = fmaxf(tmax, v);
       }
+      float mx8[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mx8[c] = __uint_as_float(sr[c]);
+#pragma unroll
+      for (int e = 8; e < 64; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], __uint_as_float(sr[e]));
+      const float traw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float tmax = traw * sl2;  // scale > 0: max commutes with it
       // P V_{j-2} must be done before P_j reuses its buffer; waiting here also
       // keeps every p_free wait below at most one phase behind.
       if (j >= 2) {
@@ -317,17 +323,17 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         l *= alpha;
         m = m_new;
       }
-      const float base = (m == -INFINITY) ? 0.f : m;
+      const float nbase = (m == -INFINITY) ? 0.f : -m;
       uint32_t pk[32];
-      float psum = 0.f;
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
-        const float p0 = ex2(__uint_as_float(sr[2 * e]) - base);
-        const float p1 = ex2(__uint_as_float(sr[2 * e + 1]) - base);
-        psum += p0 + p1;
+        const float p0 = ex2(__fmaf_rn(__uint_as_float(sr[2 * e]), sl2, nbase));
+        const float p1 = ex2(__fmaf_rn(__uint_as_float(sr[2 * e + 1]), sl2, nbase));
+        ps[e & 3] += p0 + p1;
         pk[e] = pack_bf16x2(p0, p1);
       }
-      l += psum;
+      l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
       // P_j into TMEM (its buffer was released above)
       tc_fence_after();
       tmem_st32(lane_base + TC_P0 + sb * 32, pk);
