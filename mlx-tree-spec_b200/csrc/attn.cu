@@ -394,30 +394,80 @@ __global__ void __launch_bounds__(AT_MAXW * 32, 1) tree_attn_kernel(AttnArgs a) 
 }
 
 // Merge the key splits of each output row: weights l_s * 2^(m_s - m).
-__global__ void tree_attn_combine_kernel(const float *__restrict__ part_o, const float *__restrict__ part_ml,
-                                         int splits, int rows, uint16_t *__restrict__ out,
-                                         float *__restrict__ lse) {
-  const int row = blockIdx.x;
-  const int d = threadIdx.x;  // 256 threads, one per D
-  float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) {
-    const float ll = part_ml[((size_t)s * rows + row) * 2 + 1];
-    if (ll > 0.f) m = fmaxf(m, part_ml[((size_t)s * rows + row) * 2]);
+constexpr int CB_ROWS = 4;          // query rows per combine block
+constexpr int CB_MAX_SPLITS = 256;  // split weights held in shared memory per row
+
+// Merge split-KV partials (the reference's two-pass reduce, tree_flash.py:130-143):
+// out = sum_s w_s * o_s with w_s = l_s * 2^(m_s - m) / sum_s l_s * 2^(m_s - m).
+// One warp per row computes the split weights in parallel into shared memory;
+// then 64 threads per row accumulate float4 slices with independent loads.
+__global__ void __launch_bounds__(256) tree_attn_combine_kernel(const float *__restrict__ part_o,
+                                                                const float *__restrict__ part_ml, int splits,
+                                                                int rows, uint16_t *__restrict__ out,
+                                                                float *__restrict__ lse) {
+  __shared__ float sw[CB_ROWS][CB_MAX_SPLITS];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * CB_ROWS;
+  if (warp < CB_ROWS && row0 + warp < rows) {
+    const int row = row0 + warp;
+    float m = -INFINITY;
+    for (int s = lane; s < splits; s += 32) {
+      const float2 ml = __ldg(reinterpret_cast<const float2 *>(part_ml) + (size_t)s * rows + row);
+      if (ml.y > 0.f) m = fmaxf(m, ml.x);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float den = 0.f;
+    for (int s = lane; s < splits; s += 32) {
+      const float2 ml = __ldg(reinterpret_cast<const float2 *>(part_ml) + (size_t)s * rows + row);
+      const float w = ml.y > 0.f ? ml.y * exp2f(ml.x - m) : 0.f;
+      sw[warp][s] = w;
+      den += w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    for (int s = lane; s < splits; s += 32) sw[warp][s] *= inv;
+    if (lse && lane == 0) lse[row] = den > 0.f ? (m + log2f(den)) * 0.69314718055994531f : -INFINITY;
   }
-  float num = 0.f, den = 0.f;
-  if (m != -INFINITY) {
-    for (int s = 0; s < splits; ++s) {
-      const float ms = part_ml[((size_t)s * rows + row) * 2];
-      const float ll = part_ml[((size_t)s * rows + row) * 2 + 1];
-      if (ll > 0.f) {
-        const float wgt = ll * exp2f(ms - m);
-        num += wgt * part_o[((size_t)s * rows + row) * AT_D + d];
-        den += wgt;
-      }
+  __syncthreads();
+  const int r = threadIdx.x >> 6;
+  const int row = row0 + r;
+  if (row >= rows) return;
+  const int c = (threadIdx.x & 63) * 4;
+  const float4 *po = reinterpret_cast<const float4 *>(part_o + (size_t)row * AT_D + c);
+  const size_t stride = (size_t)rows * (AT_D / 4);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __ldg(po + (size_t)(s + i) * stride);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float w = sw[r][s + i];
+      acc.x = fmaf(w, v[i].x, acc.x);
+      acc.y = fmaf(w, v[i].y, acc.y);
+      acc.z = fmaf(w, v[i].z, acc.z);
+      acc.w = fmaf(w, v[i].w, acc.w);
     }
   }
-  out[(size_t)row * AT_D + d] = float_to_bf16_bits(den > 0.f ? num / den : 0.f);
-  if (lse && d == 0) lse[row] = den > 0.f ? (m + log2f(den)) * 0.69314718055994531f : -INFINITY;
+  for (; s < splits; ++s) {
+    const float4 v = __ldg(po + (size_t)s * stride);
+    const float w = sw[r][s];
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+  }
+  *reinterpret_cast<uint2 *>(out + (size_t)row * AT_D + c) =
+      make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+}
+
+void launch_combine(const float *part_o, const float *part_ml, int splits, int rows, void *out, float *lse,
+                    cudaStream_t st) {
+  tree_attn_combine_kernel<<<(unsigned)((rows + CB_ROWS - 1) / CB_ROWS), 256, 0, st>>>(
+      part_o, part_ml, splits, rows, (uint16_t *)out, lse);
 }
 
 struct AttnPlan {
@@ -434,6 +484,7 @@ AttnPlan plan_attn(int B, int T, int Hq, int Hkv, int n_kv) {
   const int n_tiles = (n_kv + AT_KT - 1) / AT_KT;
   int splits = (sm_count() + units - 1) / units;
   if (splits > n_tiles / 2) splits = n_tiles / 2;
+  if (splits > CB_MAX_SPLITS) splits = CB_MAX_SPLITS;
   if (splits < 1) splits = 1;
   p.tiles_per_split = (n_tiles + splits - 1) / splits;
   p.splits = (n_tiles + p.tiles_per_split - 1) / p.tiles_per_split;
@@ -512,8 +563,7 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
                            (uint16_t *)out, lse, part_o, part_ml, st);
     if (r != TSB_OK) return r;
     if (splits > 1) {
-      tree_attn_combine_kernel<<<(unsigned)rows, AT_D, 0, st>>>(part_o, part_ml, splits, (int)rows,
-                                                              (uint16_t *)out, lse);
+      launch_combine(part_o, part_ml, splits, (int)rows, out, lse, st);
       if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
     }
     return TSB_OK;
@@ -565,8 +615,7 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
   }
   if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
   if (p.splits > 1) {
-    tree_attn_combine_kernel<<<(unsigned)rows, AT_D, 0, st>>>(a.part_o, a.part_ml, p.splits, (int)rows,
-                                                            (uint16_t *)out, lse);
+    launch_combine(a.part_o, a.part_ml, p.splits, (int)rows, out, lse, st);
     if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
   }
   return TSB_OK;

@@ -7,8 +7,11 @@
 // G*T query rows of a KV head (row = head_local * T + node) are contiguous in
 // q [B, Hq, T, D], so one 2D TMA box brings them; rows past the KV head's G*T
 // are computed and dropped.
-//   warp 0     TMA: Q once (four 64-wide D boxes, 128-byte swizzle), then K and
-//              V tiles of 64 keys through two rings.
+//   warp 0     TMA: Q once (four 64-wide D boxes, 128-byte swizzle), then K
+//              tiles of 64 keys through a two-stage ring.
+//   warp 6     TMA: V tiles through a three-stage ring. K and V have their own
+//              producers so a K load never queues behind a V slot that waits
+//              for O += P V.
 //   warp 1     MMA: S_j = Q K_j^T (tcgen05.mma, A = Q and B = K from shared
 //              memory, K-major, M=128, N=64, K=256) into one of two TMEM score
 //              buffers; O += P_j V_j with P_j from TMEM and V_j from shared
@@ -34,8 +37,8 @@ constexpr int TC_QBOX = 128 * 128;              // one 64-wide D box of 128 rows
 constexpr int TC_KVBOX = TC_KT * 128;           // one 64-wide D box of 64 keys
 constexpr int TC_Q_BYTES = 4 * TC_QBOX;         // 64 KB
 constexpr int TC_KV_BYTES = 4 * TC_KVBOX;       // 32 KB per K or V tile
-constexpr int TC_NK = 2, TC_NV = 2;
-constexpr int TC_THREADS = 192;
+constexpr int TC_NK = 2, TC_NV = 3;
+constexpr int TC_THREADS = 224;
 constexpr size_t TC_SMEM = TC_Q_BYTES + (TC_NK + TC_NV) * TC_KV_BYTES + 1024 + 1024;
 constexpr uint32_t TC_O = 0, TC_S0 = 256, TC_P0 = 384;
 constexpr float TC_RESCALE_LOG2 = 8.f;
@@ -87,6 +90,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
   uint64_t *p_full = s_free + 2, *p_free = p_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(p_free + 2);
   unsigned long long *sBits = reinterpret_cast<unsigned long long *>(tmem_slot + 2);  // [T <= 64]
+  int32_t *sPar = reinterpret_cast<int32_t *>(sBits + 64);                            // [T <= 64]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int G = a.Hq / a.Hkv;
@@ -116,25 +120,6 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     fence_mbar_init();
     fence_proxy_async_smem();
   }
-  // node masks, from the parent array or given
-  for (int node = threadIdx.x; node < a.T; node += blockDim.x) {
-    unsigned long long m = 0;
-    if (a.parents) {
-      const int32_t *p = a.parents + (size_t)b * a.T;
-      int j = node;
-      bool ok = true;
-      for (int steps = 0; steps <= a.T && j != -1; ++steps) {
-        m |= 1ull << j;
-        const int pj = p[j];
-        if (!(pj == -1 || (pj >= 0 && pj < j))) { ok = false; break; }
-        j = pj;
-      }
-      if (!ok) m = 0;
-    } else {
-      m = a.bits[(size_t)b * a.T + node];
-    }
-    sBits[node] = m;
-  }
   if (warp == 0) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -155,42 +140,44 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       mbar_arrive_expect_tx(q_full, TC_Q_BYTES);
 #pragma unroll
       for (int d = 0; d < 4; ++d) tma_load_2d(sQ + d * TC_QBOX, &tmap_q, d * 64, qrow, q_full);
-      int ik = 0, iv = 0;
       bool ok = true;
-      // K runs up to two tiles ahead of V (the MMA needs K_{j+1} before V_j)
-      for (int j = 0; j < nt && ok; ++j) {
+      int j = 0;
+      for (; j < nt && ok; ++j) {
         const int key0 = (int)kv_row0 + (j_begin + j) * TC_KT;
-        {
-          const int s = ik % TC_NK;
-          if (ik >= TC_NK && !mbar_wait(&k_free[s], ((ik / TC_NK) - 1) & 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[s], TC_KV_BYTES);
+        const int st = j % TC_NK;
+        if (j >= TC_NK && !mbar_wait(&k_free[st], ((j / TC_NK) - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&k_full[st], TC_KV_BYTES);
 #pragma unroll
-          for (int d = 0; d < 4; ++d)
-            tma_load_2d(sK + s * TC_KV_BYTES + d * TC_KVBOX, &tmap_k, d * 64, key0, &k_full[s]);
-          ++ik;
-        }
-        {
-          const int s = iv % TC_NV;
-          if (iv >= TC_NV && !mbar_wait(&v_free[s], ((iv / TC_NV) - 1) & 1)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[s], TC_KV_BYTES);
-#pragma unroll
-          for (int d = 0; d < 4; ++d)
-            tma_load_2d(sV + s * TC_KV_BYTES + d * TC_KVBOX, &tmap_v, d * 64, key0, &v_full[s]);
-          ++iv;
-        }
+        for (int d = 0; d < 4; ++d)
+          tma_load_2d(sK + st * TC_KV_BYTES + d * TC_KVBOX, &tmap_k, d * 64, key0, &k_full[st]);
       }
       // drain: the issued loads have landed before the CTA can exit
       const unsigned long long t0 = globaltimer_ns();
       while (!mbar_try_wait(q_full, 0)) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
       }
-      for (int i = (ik > TC_NK ? ik - TC_NK : 0); i < ik; ++i) {
+      for (int i = (j > TC_NK ? j - TC_NK : 0); i < j; ++i) {
         const unsigned long long t1 = globaltimer_ns();
         while (!mbar_try_wait(&k_full[i % TC_NK], (i / TC_NK) & 1)) {
           if (globaltimer_ns() - t1 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
         }
       }
-      for (int i = (iv > TC_NV ? iv - TC_NV : 0); i < iv; ++i) {
+    }
+  } else if (warp == 6) {
+    // ---------------- V producer
+    if (elect_one()) {
+      bool ok = true;
+      int j = 0;
+      for (; j < nt && ok; ++j) {
+        const int key0 = (int)kv_row0 + (j_begin + j) * TC_KT;
+        const int st = j % TC_NV;
+        if (j >= TC_NV && !mbar_wait(&v_free[st], ((j / TC_NV) - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&v_full[st], TC_KV_BYTES);
+#pragma unroll
+        for (int d = 0; d < 4; ++d)
+          tma_load_2d(sV + st * TC_KV_BYTES + d * TC_KVBOX, &tmap_v, d * 64, key0, &v_full[st]);
+      }
+      for (int i = (j > TC_NV ? j - TC_NV : 0); i < j; ++i) {
         const unsigned long long t1 = globaltimer_ns();
         while (!mbar_try_wait(&v_full[i % TC_NV], (i / TC_NV) & 1)) {
           if (globaltimer_ns() - t1 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
@@ -247,6 +234,31 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     }
   } else {
     // ---------------- softmax / epilogue (thread = query row = TMEM lane)
+    // node masks, from the parent array (staged in shared memory) or given;
+    // built here, off the producers' path, while the first scores compute
+    {
+      const int st = threadIdx.x - 64;  // 0..127
+      if (st < a.T) sPar[st] = a.parents ? a.parents[(size_t)b * a.T + st] : 0;
+      named_barrier_sync(1, 128);
+      if (st < a.T) {
+        unsigned long long m = 0;
+        if (a.parents) {
+          int j = st;
+          bool okp = true;
+          for (int steps = 0; steps <= a.T && j != -1; ++steps) {
+            m |= 1ull << j;
+            const int pj = sPar[j];
+            if (!(pj == -1 || (pj >= 0 && pj < j))) { okp = false; break; }
+            j = pj;
+          }
+          if (!okp) m = 0;
+        } else {
+          m = a.bits[(size_t)b * a.T + st];
+        }
+        sBits[st] = m;
+      }
+      named_barrier_sync(1, 128);
+    }
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const int gr = rb * 128 + r;
@@ -404,6 +416,7 @@ void plan_attn_tc(int B, int T, int Hq, int Hkv, int n_kv, int &row_blocks, int 
   const int n_tiles = (n_kv + TC_KT - 1) / TC_KT;
   int s = sm_count() / units;  // one CTA per SM (TMEM 512 columns): stay within one wave
   if (s > n_tiles / 4) s = n_tiles / 4;
+  if (s > 256) s = 256;  // the combine kernel holds at most 256 split weights per row
   if (s < 1) s = 1;
   tiles_per_split = (n_tiles + s - 1) / s;
   splits = (n_tiles + tiles_per_split - 1) / tiles_per_split;

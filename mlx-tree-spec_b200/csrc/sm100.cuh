@@ -80,6 +80,8 @@ TSB_HD bool warp_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------- proxies / fences
+// Barrier among `count` threads (whole warps) of the CTA, id 1..15.
+TSB_HD void named_barrier_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
 TSB_HD void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---------------------------------------------------------------- TMA
