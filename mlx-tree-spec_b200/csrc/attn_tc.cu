@@ -7,24 +7,28 @@
 // G*T query rows of a KV head (row = head_local * T + node) are contiguous in
 // q [B, Hq, T, D], so one 2D TMA box brings them; rows past the KV head's G*T
 // are computed and dropped.
-//   warp 0     TMA: Q once (four 64-wide D boxes, 128-byte swizzle), then K
-//              tiles of 64 keys through a two-stage ring.
-//   warp 6     TMA: V tiles through a three-stage ring. K and V have their own
+//   warp 0     TMA: Q once (four 64-wide D boxes, 128-byte swizzle, staged in
+//              two V slots), then K tiles of 64 keys through a three-stage ring.
+//   warp 6     TMA: V tiles through a four-stage ring. K and V have their own
 //              producers so a K load never queues behind a V slot that waits
-//              for O += P V.
-//   warp 1     MMA: S_j = Q K_j^T (tcgen05.mma, A = Q and B = K from shared
-//              memory, K-major, M=128, N=64, K=256) into one of two TMEM score
-//              buffers; O += P_j V_j with P_j from TMEM and V_j from shared
+//              for O += P V; V loads into the two staging slots wait until Q
+//              has moved to tensor memory.
+//   warp 1     MMA: S_j = Q K_j^T with Q from TMEM (A operand) and K from shared
+//              memory (K-major, M=128, N=64, K=256), so a tile reads only K from
+//              shared memory; O += P_j V_j with P_j from TMEM and V_j from shared
 //              memory as an MN-major operand (M=128, N=256, K=64). S_{j+1} is
 //              issued before O += P_j V_j so scores overlap the softmax.
-//   warps 2-5  softmax, one thread per query row (= TMEM lane): scores ->
-//              scale, ancestor mask, online max/sum in the exp2 domain -> P as
-//              bf16 into TMEM. O is rescaled in TMEM only when the running max
-//              grows by more than 2^8 (values stay bounded in between), after
-//              the previous P V has completed. Epilogue: O / l -> bf16 out, or
-//              normalised partials plus (max, sum) for the combine kernel.
-// TMEM (512 columns): O [0, 256), S0 [256, 320), S1 [320, 384), P0 [384, 416),
-// P1 [416, 448).
+//   warps 2-5  copy Q into TMEM once; then softmax, one thread per query row
+//              (= TMEM lane): scores -> scale, ancestor mask, online max/sum in
+//              the exp2 domain -> P as bf16 written over the first 32 columns of
+//              its own score buffer. O is rescaled in TMEM only when the running
+//              max grows by more than 2^8 (values stay bounded in between),
+//              after the previous P V has completed. Epilogue: O / l -> bf16
+//              out, or normalised partials plus (max, sum) for the combine.
+// TMEM (512 columns): O [0, 256), Q [256, 384), S0 [384, 448), S1 [448, 512);
+// P_j lives in S_{j&1} [0, 32). S_{j+2} overwrites P_j only after O += P_j V_j:
+// it is issued after that MMA, and tcgen05.mma operations of one thread run in
+// issue order.
 #include "sm100.cuh"
 
 namespace tsb {
@@ -37,10 +41,11 @@ constexpr int TC_QBOX = 128 * 128;              // one 64-wide D box of 128 rows
 constexpr int TC_KVBOX = TC_KT * 128;           // one 64-wide D box of 64 keys
 constexpr int TC_Q_BYTES = 4 * TC_QBOX;         // 64 KB
 constexpr int TC_KV_BYTES = 4 * TC_KVBOX;       // 32 KB per K or V tile
-constexpr int TC_NK = 2, TC_NV = 3;
+constexpr int TC_NK = 3, TC_NV = 4;
 constexpr int TC_THREADS = 224;
-constexpr size_t TC_SMEM = TC_Q_BYTES + (TC_NK + TC_NV) * TC_KV_BYTES + 1024 + 1024;
-constexpr uint32_t TC_O = 0, TC_S0 = 256, TC_P0 = 384;
+constexpr size_t TC_SMEM = (TC_NK + TC_NV) * TC_KV_BYTES + 1024 + 1024;
+constexpr int TC_Q_SLOT = 2;                  // V slots TC_Q_SLOT, TC_Q_SLOT+1 stage Q
+constexpr uint32_t TC_O = 0, TC_Q = 256, TC_S0 = 384;
 constexpr float TC_RESCALE_LOG2 = 8.f;
 
 struct TcArgs {
@@ -79,12 +84,12 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char *sQ = smem;
-  unsigned char *sK = sQ + TC_Q_BYTES;
+  unsigned char *sK = smem;
   unsigned char *sV = sK + TC_NK * TC_KV_BYTES;
+  unsigned char *sQ = sV + TC_Q_SLOT * TC_KV_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(sV + TC_NV * TC_KV_BYTES);
-  uint64_t *q_full = bars;
-  uint64_t *k_full = bars + 1, *k_free = k_full + TC_NK;
+  uint64_t *q_full = bars, *q_done = bars + 1;
+  uint64_t *k_full = bars + 2, *k_free = k_full + TC_NK;
   uint64_t *v_full = k_free + TC_NK, *v_free = v_full + TC_NV;
   uint64_t *s_full = v_free + TC_NV, *s_free = s_full + 2;
   uint64_t *p_full = s_free + 2, *p_free = p_full + 2;
@@ -109,6 +114,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_done, 4);
     for (int i = 0; i < TC_NK; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_free[i], 1); }
     for (int i = 0; i < TC_NV; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_free[i], 1); }
     for (int i = 0; i < 2; ++i) {
@@ -171,6 +177,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       for (; j < nt && ok; ++j) {
         const int key0 = (int)kv_row0 + (j_begin + j) * TC_KT;
         const int st = j % TC_NV;
+        if (j == TC_Q_SLOT && !mbar_wait(q_done, 0)) { ok = false; break; }
         if (j >= TC_NV && !mbar_wait(&v_free[st], ((j / TC_NV) - 1) & 1)) { ok = false; break; }
         mbar_arrive_expect_tx(&v_full[st], TC_KV_BYTES);
 #pragma unroll
@@ -188,19 +195,18 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     // ---------------- MMA issuer
     const uint32_t idesc_s = idesc_bf16_f32(128, TC_KT);
     const uint32_t idesc_o = idesc_bf16_f32(128, TC_D) | (1u << 16);  // B (V) MN-major
-    bool ok = warp_wait(q_full, 0);
+    bool ok = warp_wait(q_done, 0);
     auto issue_s = [&](int j) -> bool {
       const int s = j % TC_NK, sb = j & 1;
       if (!warp_wait(&k_full[s], (j / TC_NK) & 1)) return false;
       if (j >= 2 && !warp_wait(&s_free[sb], ((j >> 1) - 1) & 1)) return false;
       tc_fence_after();
       if (elect_one()) {
-        const uint32_t qa = smem_addr(sQ), kb = smem_addr(sK + s * TC_KV_BYTES);
+        const uint32_t kb = smem_addr(sK + s * TC_KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
-          const uint32_t off_q = (kk >> 2) * TC_QBOX + (kk & 3) * 32;
           const uint32_t off_k = (kk >> 2) * TC_KVBOX + (kk & 3) * 32;
-          mma_ss_f16(tmem + TC_S0 + sb * 64, desc_kmajor_sw128(qa + off_q), desc_kmajor_sw128(kb + off_k), idesc_s,
+          mma_ts_f16(tmem + TC_S0 + sb * 64, tmem + TC_Q + kk * 8, desc_kmajor_sw128(kb + off_k), idesc_s,
                      kk > 0 ? 1u : 0u);
         }
         mma_commit(&s_full[sb]);
@@ -218,7 +224,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         const uint32_t vb = smem_addr(sV + s * TC_KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < TC_KT / 16; ++kk) {
-          mma_ts_f16(tmem + TC_O, tmem + TC_P0 + pb * 32 + kk * 8, desc_mnmajor_sw128(vb + kk * 2048, TC_KVBOX),
+          mma_ts_f16(tmem + TC_O, tmem + TC_S0 + pb * 64 + kk * 8, desc_mnmajor_sw128(vb + kk * 2048, TC_KVBOX),
                      idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&v_free[s]);
@@ -269,7 +275,26 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
     const float sl2 = a.scale_log2;
     const int n_kv = a.n_kv;
     float m = -INFINITY, l = 0.f;  // running max (log2 domain) and sum
-    bool ok = true;
+    // Q row r -> TMEM lane r, columns TC_Q + d/2 (the A-operand layout of a K-major
+    // M=128 tile); the staging slots then go back to the V ring
+    bool ok = warp_wait(q_full, 0);
+    if (ok) {
+#pragma unroll 1
+      for (int bx = 0; bx < 4; ++bx) {
+        const unsigned char *row = sQ + bx * TC_QBOX + r * 128;
+        uint32_t qv[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 u = *reinterpret_cast<const uint4 *>(row + ((c ^ (r & 7)) << 4));
+          qv[4 * c] = u.x; qv[4 * c + 1] = u.y; qv[4 * c + 2] = u.z; qv[4 * c + 3] = u.w;
+        }
+        tmem_st32(lane_base + TC_Q + bx * 32, qv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_done);
+    }
     for (int j = 0; j < nt && ok; ++j) {
       const int sb = j & 1;
       ok = warp_wait(&s_full[sb], (j >> 1) & 1);
@@ -306,7 +331,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       const float traw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float tmax = traw * sl2;  // scale > 0: max commutes with it
-      // P V_{j-2} must be done before P_j reuses its buffer; waiting here also
+      // P V_{j-2} is done (S_j, written after it, is complete); waiting here
       // keeps every p_free wait below at most one phase behind.
       if (j >= 2) {
         ok = warp_wait(&p_free[sb], ((j >> 1) - 1) & 1);
@@ -346,9 +371,9 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         pk[e] = pack_bf16x2(p0, p1);
       }
       l += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      // P_j into TMEM (its buffer was released above)
+      // P_j into TMEM, over the scores it was made from
       tc_fence_after();
-      tmem_st32(lane_base + TC_P0 + sb * 32, pk);
+      tmem_st32(lane_base + TC_S0 + sb * 64, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
