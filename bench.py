@@ -180,6 +180,30 @@ def copies_needed(ns, k, l2_bytes=126 * 2**20, factor=2.5):
 
 # ------------------------------------------------------------------ tsb arm
 
+def run_profile_attn(args):
+    """Config-4 tree attention (B=1, L=32768, T=32, 24q/4kv, D=256, bf16 KV): --warmup calls, then one."""
+    import numpy as np
+    import torch
+
+    import tsb
+    from oracle import gen
+
+    torch.cuda.set_device(0)
+    tsb.load_library()
+    bsz, L, t, hq, hkv, d = 1, 32768, 32, 24, 4, 256
+    n_kv = L + t
+    g = torch.Generator(device="cuda").manual_seed(3)
+    k = torch.randn(bsz, hkv, n_kv, d, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(bsz, hkv, n_kv, d, device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn(bsz, hq, t, d, device="cuda", generator=g).to(torch.bfloat16)
+    parents = torch.from_numpy(np.stack([gen.tree_parents(np.random.default_rng(i), t) for i in range(bsz)])).cuda()
+    cache = tsb.KVCache(k, v, n_kv)
+    for _ in range(args.warmup + 1):
+        tsb.tree_flash(q, cache, d**-0.5, parents=parents)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "attn", "calls": args.warmup + 1}))
+
+
 def run_tsb(args):
     import numpy as np
     import torch
@@ -222,6 +246,12 @@ def run_tsb(args):
         step(i)
     torch.cuda.synchronize()
     barrier(world)
+    if args.profile == "qmm":
+        step(args.warmup)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"profile": "qmm", "launches_per_step": len(calls), "warmup_steps": args.warmup}))
+        return
 
     # CUDA graph of one step (kernel launches only; collectives use NCCL in-graph)
     g = torch.cuda.CUDAGraph()
@@ -465,16 +495,21 @@ def run_secondary(pool, xs, hbm_peak, bf16_peak):
                                           "TFLOP/s": round(fl / us / 1e6, 1),
                                           "frac_hbm": round(byts / us / 1e3 / hbm_peak, 4)}
         del caches
-    # unmasked FlashAttention comparator (torch SDPA, same shape, bf16)
+    # unmasked attention comparator: torch SDPA on the same shape and the same 4 KV
+    # heads (enable_gqa), bf16, no mask, K/V rotating through 4 caches like ours
     try:
         bsz, L, t, hq, hkv, d = 1, 32768, 32, 24, 4, 256
-        kk = [torch.randn(bsz, hq, L + t, d, device="cuda").to(torch.bfloat16) for _ in range(2)]
+        kv = [(torch.randn(bsz, hkv, L + t, d, device="cuda").to(torch.bfloat16),
+               torch.randn(bsz, hkv, L + t, d, device="cuda").to(torch.bfloat16)) for _ in range(4)]
         q = torch.randn(bsz, hq, t, d, device="cuda").to(torch.bfloat16)
-        us = time_graph(lambda: [torch.nn.functional.scaled_dot_product_attention(q, k_, k_) for k_ in kk]) / 2
-        out["sdpa_unmasked_B1_L32768_bf16_fullheads"] = {"us": round(us, 2), "note": "torch SDPA, K/V expanded to 24 heads"}
-        del kk
+        sdpa = torch.nn.functional.scaled_dot_product_attention
+        us = time_graph(lambda: [sdpa(q, k_, v_, enable_gqa=True) for (k_, v_) in kv]) / len(kv)
+        byts = bsz * (L + t) * hkv * 512 * 2 + 2 * bsz * t * hq * d * 2
+        out["sdpa_gqa_unmasked_B1_L32768_bf16"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1),
+                                                   "note": "torch scaled_dot_product_attention, enable_gqa, no mask"}
+        del kv
     except Exception as e:  # pragma: no cover - comparator only
-        out["sdpa_unmasked"] = {"error": str(e)[:120]}
+        out["sdpa_gqa_unmasked"] = {"error": str(e)[:160]}
     return out
 
 
@@ -555,11 +590,16 @@ def main():
     ap.add_argument("--impl", choices=["tsb", "reference"], default="tsb")
     ap.add_argument("--no-secondary", dest="secondary", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--profile", choices=["qmm", "attn"], default=None,
+                    help="profiling driver for ncu: --warmup eager steps, then exactly one eager step "
+                         "(qmm: the 15 sweep calls; attn: one config-4 B=1 L=32768 bf16 call); no timing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile == "attn":
+        run_profile_attn(args)
     else:
         run_tsb(args)
 

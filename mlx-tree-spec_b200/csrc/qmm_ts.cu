@@ -12,29 +12,41 @@
 // shared-memory path for the packed codes and x only.
 //
 // CTA: 128 weight rows (one TMEM lane each) x all tokens (NP = M rounded up
-// to 16), a K range of whole stages; split-K CTAs of one row tile form a
-// cluster and reduce through distributed shared memory. Warp roles:
-//   warp 0    TMA producer of the codes ring: per stage (4 groups = 256 K)
-//             the codes of the 128 rows (32 words each, 128-byte swizzle) and
-//             their scales and biases (8-group boxes). A slot is refilled as
-//             soon as the dequantizers have loaded its words into registers.
-//   warp 10   TMA producer of the x ring: x for the stage (four 64-K boxes of
+// to 16), a K range of whole stages (4 groups = 256 K each); one CTA per SM
+// (all 512 TMEM columns); split-K CTAs of one row tile form a cluster and
+// reduce through distributed shared memory. Warp roles:
+//   warp 0    TMA producer of the codes ring: per stage the codes of the 128
+//             rows (32 words each, 128-byte swizzle) and their scales and
+//             biases (8-group boxes). A slot is refilled as soon as its
+//             dequantizers have loaded its words into registers.
+//   warp 2    TMA producer of the x ring: x for the stage (four 64-K boxes of
 //             NP rows, 128-byte swizzle, rows >= M zero-filled by TMA); a slot
 //             is refilled when the MMAs that read it have completed.
-//   warp 1    MMA issuer: per group 4 tcgen05.mma (M=128, N=NP, K=16) on the
-//             scaled codes plus 4 on the group's bias (below); A from TMEM,
-//             B = x from shared memory, f32 accumulator in TMEM.
-//   warps 2-9 dequantizers, two warpgroups (warpgroup w takes groups 2w and
-//             2w+1 of each stage; thread = weight row = TMEM lane): codes ->
-//             bf16(s*q) -> tcgen05.st into a ring of per-group A slots; the
-//             store of one group drains while the next is dequantized. Then
-//             the epilogue (TMEM -> registers -> bf16 y, or split-K partials).
+//   warps 1,3,5,7 MMA issuers (one lane each; two for NP = 128): per stage
+//             one wait, 4 (or 8) tcgen05.mma (M=128, N=NP, K=16) back to back
+//             and two commits; issuer u takes its share of each stage's groups
+//             into accumulator u (summed in the epilogue). A = the dequantized
+//             weights from TMEM, B = x from shared memory, f32 accumulators in
+//             TMEM. At N <= 64 an MMA costs ~27 ns whatever N is, so the issue
+//             loop carries no per-group synchronization.
+//   warps 8-23 dequantizers, four warpgroups; warpgroup w takes group w of
+//             every stage (thread = weight row = TMEM lane): codes ->
+//             bf16(s*q + b) -> tcgen05.st into a ring of stage slots in TMEM
+//             (4 groups each); a stage's store drains behind the next
+//             stage's arithmetic before it is handed to the MMA. One barrier
+//             pair per stage slot: all 16 dequantizer
+//             warps arrive on a_full, the MMA commits a_empty once per stage,
+//             and every waiter walks the stages in order, so no wait can run
+//             two phases ahead.
+//             Warpgroup 0 then runs the epilogue (TMEM -> registers -> bf16 y,
+//             or split-K partials).
 //
-// Arithmetic: y = sum_g [ sum_{k in g} bf16(s q_k) x_k + b sum_{k in g} x_k ].
-// The first term needs one bf16x2 fma per pair of weights (fma(128+q, s,
-// -128 s), exactly rounded). The second is the reference's `b * sum x` term
-// (qmm_packed.py:14-16, 424-425) done on the tensor core: an 8-column TMEM
-// block holding b in all 16 K positions multiplies each 16-wide K slice of x.
+// Arithmetic: y = sum_k w_k x_k with w = bf16(fma(q, s, b)), the reference's
+// dequantization rule (qmm_packed.py:200, 348, 635) exactly: (code | 0x4300)
+// is bf16 128 + q, one bf16x2 subtract gives q exactly and one fused bf16x2
+// fma rounds q*s + b once. At N = NP <= 64 the MMA is bound by fetching its A
+// operand from TMEM (4 KB per instruction whatever N is), so the weights carry
+// the bias and each group costs only its four K=16 MMAs.
 #include "sm100.cuh"
 
 #include <cooperative_groups.h>
@@ -55,23 +67,26 @@ struct TsCfg {
   static constexpr int CSLOT_BYTES = C_BYTES + 2 * SB_BYTES;
   static constexpr int X_BOX_BYTES = NP * 128;     // one 64-K box of x
   static constexpr int XSLOT_BYTES = SG * X_BOX_BYTES;
-  // ring depths; two CTAs per SM up to NP = 64 (shared memory and 256 TMEM
-  // columns each), one for NP = 128
-  static constexpr int NC = NP == 64 ? 2 : 3;      // codes slots
-  static constexpr int NX = NP == 16 ? 4 : 2;      // x slots
+  static constexpr int RING_BUDGET = 225 * 1024;   // shared memory for the two rings
+  static constexpr int NX = NP <= 32 ? 4 : (NP == 64 ? 3 : 2);                 // x slots
+  static constexpr int NC_FIT = (RING_BUDGET - NX * XSLOT_BYTES) / CSLOT_BYTES;
+  static constexpr int NC = NC_FIT > 12 ? 12 : NC_FIT;                        // codes slots
   static constexpr int X_AREA = NC * CSLOT_BYTES;
   static constexpr int STAGE_AREA = X_AREA + NX * XSLOT_BYTES;
-  static constexpr int A_COL0 = NP < 32 ? 32 : NP; // D in columns [0, NP), A slots after
-  static constexpr int GA = 40;                    // per group slot: 32 columns s*q, 8 columns bias
-  static constexpr int TMEM_COLS = NP <= 64 ? 256 : 512;
+  static constexpr int NI = NP <= 64 ? 4 : 2;      // MMA issuers, one accumulator each
+  static constexpr int A_COL0 = NI * NP < 32 ? 32 : NI * NP;  // accumulators in [0, NI NP), A slots after
+  static constexpr int GA = 32;                    // per group slot: 64 bf16 weights per row
+  static constexpr int TMEM_COLS = 512;
   static constexpr int NAG_FIT = (TMEM_COLS - A_COL0) / GA;
-  static constexpr int NAG = NAG_FIT > 8 ? 8 : NAG_FIT;  // ring of per-group A slots in TMEM
-  static constexpr int THREADS = 352;
+  static constexpr int NAS = (NAG_FIT > 12 ? 12 : NAG_FIT) / SG;  // stage slots of A in TMEM (4 groups each)
+  static constexpr int WGS = 4;                    // dequantizer warpgroups
+  static constexpr int DQ_WARP0 = 8;               // first dequantizer warp (lane quarter = warp & 3)
+  static constexpr int THREADS = (DQ_WARP0 + 4 * WGS) * 32;
   static constexpr size_t SMEM = (size_t)STAGE_AREA + 1024 + 1024;
-  static_assert(NAG >= 4, "A ring");
+  static_assert(NC >= 4 && NAS >= 2, "ring depths");
   static_assert(CSLOT_BYTES % 1024 == 0 && XSLOT_BYTES % 1024 == 0, "slot alignment (128-byte swizzle atoms)");
   static_assert(NP * 512 <= STAGE_AREA, "split-K partials fit in the stage area");
-  static_assert(SMEM <= (NP <= 64 ? 112 * 1024 : 200 * 1024), "shared memory per CTA");
+  static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
 // Advance a ring position (slot, phase bit) without divisions.
@@ -84,7 +99,7 @@ struct Ring {
 };
 
 template <int NP>
-__global__ void __launch_bounds__(352, NP <= 64 ? 2 : 1)
+__global__ void __launch_bounds__(TsCfg<NP>::THREADS, 1)
 qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
               const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b,
               const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases,
@@ -98,9 +113,9 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   uint64_t *free_c = bars + C::NC;               // [NC] dequantizers have loaded the slot
   uint64_t *full_x = bars + 2 * C::NC;           // [NX] x landed
   uint64_t *free_x = full_x + C::NX;             // [NX] MMAs that read the slot are done
-  uint64_t *a_full = free_x + C::NX;             // [NAG] group written into TMEM
-  uint64_t *a_empty = a_full + C::NAG;           // [NAG] MMA done with the slot
-  uint64_t *acc_full = a_empty + C::NAG;
+  uint64_t *a_full = free_x + C::NX;             // [NAS] stage written into TMEM
+  uint64_t *a_empty = a_full + C::NAS;           // [NAS] MMA done with the stage slot
+  uint64_t *acc_full = a_empty + C::NAS;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -121,17 +136,17 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NC; ++s) {
       mbar_init(&full_c[s], 1);
-      mbar_init(&free_c[s], 8);  // every dequantizer warp
+      mbar_init(&free_c[s], 16);  // every dequantizer warp
     }
     for (int s = 0; s < C::NX; ++s) {
       mbar_init(&full_x[s], 1);
-      mbar_init(&free_x[s], 1);
+      mbar_init(&free_x[s], C::NI);  // every MMA issuer
     }
-    for (int b = 0; b < C::NAG; ++b) {
-      mbar_init(&a_full[b], 4);  // the 4 warps of the group's warpgroup
-      mbar_init(&a_empty[b], 1);
+    for (int b = 0; b < C::NAS; ++b) {
+      mbar_init(&a_full[b], 16);  // every dequantizer warp
+      mbar_init(&a_empty[b], C::NI);
     }
-    mbar_init(acc_full, 1);
+    mbar_init(acc_full, C::NI);
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -146,8 +161,8 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   auto cslot = [&](int s) { return smem + (size_t)s * C::CSLOT_BYTES; };
   auto xslot = [&](int s) { return smem + C::X_AREA + (size_t)s * C::XSLOT_BYTES; };
 
-  if (warp == 0 || warp == 10) {
-    // ---------------- TMA producers: warp 0 the codes ring, warp 10 the x ring
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers: warp 0 the codes ring, warp 2 the x ring
     const bool codes = warp == 0;
     const int nslots = codes ? C::NC : C::NX;
     uint64_t *full = codes ? full_c : full_x;
@@ -193,143 +208,134 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer
-    const uint32_t idesc = idesc_bf16_f32(128, NP);
-    bool ok = true;
-    Ring ring, aring;
-    int gi = 0;
-    for (int i = 0; i < nst && ok; ++i, ring.next(C::NX)) {
-      ok = warp_wait(&full_x[ring.slot], ring.phase);
-      if (!ok) break;
-      const int gs = g0 + i * C::SG;
-      const uint32_t xs = smem_addr(xslot(ring.slot));
-      for (int gl = 0; gl < C::SG && gs + gl < g1; ++gl, ++gi, aring.next(C::NAG)) {
-        ok = warp_wait(&a_full[aring.slot], aring.phase);
+  } else if ((warp & 1) && warp < 2 * C::NI) {
+    // ---------------- MMA issuers: warp 2u+1 takes groups [u, u+1) * SG/NI of
+    // every stage into accumulator u (independent MMA streams keep the tensor
+    // pipe busier than one dependent chain); one lane each, descriptors built
+    // once per stage and advanced by adding the 16-byte-unit offset of each
+    // 64-K box and 16-K slice
+    const int u = warp >> 1;
+    constexpr int GPI = C::SG / C::NI;  // groups per issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, NP);
+      const uint32_t dacc = tmem_base + (uint32_t)(u * NP);
+      bool ok = true, first = true;
+      Ring ring, aring;
+      for (int i = 0; i < nst && ok; ++i, ring.next(C::NX), aring.next(C::NAS)) {
+        ok = mbar_wait(&full_x[ring.slot], ring.phase) && mbar_wait(&a_full[aring.slot], aring.phase);
         if (!ok) break;
         tc_fence_after();
-        if (elect_one()) {
-          const uint32_t a_grp = tmem_base + C::A_COL0 + aring.slot * C::GA;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bd = desc_kmajor_sw128(xs + gl * C::X_BOX_BYTES + kk * 32);
-            mma_ts_f16(tmem_base, a_grp + kk * 8, bd, idesc, (gi > 0 || kk > 0) ? 1u : 0u);
-            mma_ts_f16(tmem_base, a_grp + 32, bd, idesc, 1u);  // + b * (sum of this x slice)
-          }
-          mma_commit(&a_empty[aring.slot]);
+        const int gs = g0 + i * C::SG;
+        const int gend = min(GPI * (u + 1), g1 - gs);
+        const uint64_t xd = desc_kmajor_sw128(smem_addr(xslot(ring.slot)));
+        const uint32_t a0 = tmem_base + C::A_COL0 + aring.slot * C::SG * C::GA;
+        for (int gl = GPI * u; gl < gend; ++gl) {
+          const uint32_t ag = a0 + gl * C::GA;
+          const uint64_t bd = xd + (uint64_t)((gl * C::X_BOX_BYTES) >> 4);
+          mma_ts_f16(dacc, ag, bd, idesc, first ? 0u : 1u);
+          mma_ts_f16(dacc, ag + 8, bd + 2, idesc, 1u);  // +32 B: next 16 K
+          mma_ts_f16(dacc, ag + 16, bd + 4, idesc, 1u);
+          mma_ts_f16(dacc, ag + 24, bd + 6, idesc, 1u);
+          first = false;
         }
-        __syncwarp();
-      }
-      if (!ok) break;
-      if (elect_one()) {
+        mma_commit(&a_empty[aring.slot]);
         mma_commit(&free_x[ring.slot]);
         if (i == nst - 1) mma_commit(acc_full);
       }
-      __syncwarp();
     }
-  } else {
+    __syncwarp();
+  } else if (warp >= C::DQ_WARP0) {
     // ---------------- dequantizers (thread = weight row = TMEM lane)
     const int q = warp & 3;
-    const int wg = (warp - 2) >> 2;  // groups 2wg, 2wg+1 of each stage
+    const int wg = (warp - C::DQ_WARP0) >> 2;  // group wg of every stage
     const int r = q * 32 + lane;
     const int row = n0 + r;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     bool ok = true;
-    int pend_slot = -1;  // A slot whose TMEM store is in flight
+    int pend = -1;  // stage slot whose TMEM store is still draining
     auto flush = [&]() {
-      if (pend_slot >= 0) {
+      if (pend >= 0) {
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[pend_slot]);
-        pend_slot = -1;
+        if (lane == 0) mbar_arrive(&a_full[pend]);
+        pend = -1;
       }
     };
-    // A slots: group gi of the CTA uses slot gi % NAG; this warpgroup's groups
-    // are gi = 4i + 2wg + {0, 1}.
-    Ring aring;
-    aring.slot = (2 * wg) % C::NAG;
-    aring.phase = (uint32_t)((2 * wg) / C::NAG) & 1u;
-    uint32_t abuf[2][32];
-    Ring ring;
-    for (int i = 0; i < nst && ok; ++i, ring.next(C::NC)) {
+    Ring ring, aring;
+    for (int i = 0; i < nst && ok; ++i, ring.next(C::NC), aring.next(C::NAS)) {
       ok = warp_wait(&full_c[ring.slot], ring.phase);
       if (!ok) break;
       const int gs = g0 + i * C::SG;
+      const int g = gs + wg;
+      const bool have = g < g1;  // uniform across the warpgroup
       const unsigned char *st = cslot(ring.slot);
-      // this row's scales and biases of the two groups (one 32-bit load each)
-      uint32_t s_pair, b_pair;
+      // this row's scale and bias of the group
+      uint32_t sbits = 0, bbits = 0;
       if (sb_direct) {
-        const int ga = gs + 2 * wg;
-        const size_t idx = (size_t)row * G + ga;
-        const bool v0 = ga < g1, v1 = ga + 1 < g1;
-        s_pair = (v0 ? uint32_t(__ldg(scales + idx)) : 0u) | (v1 ? uint32_t(__ldg(scales + idx + 1)) << 16 : 0u);
-        b_pair = (v0 ? uint32_t(__ldg(biases + idx)) : 0u) | (v1 ? uint32_t(__ldg(biases + idx + 1)) << 16 : 0u);
-      } else {
-        const int off = r * 16 + ((gs & 7) + 2 * wg) * 2;
-        s_pair = *reinterpret_cast<const uint32_t *>(st + C::C_BYTES + off);
-        b_pair = *reinterpret_cast<const uint32_t *>(st + C::C_BYTES + C::SB_BYTES + off);
-      }
-      // both groups' packed words into registers, then release the codes slot
-      uint32_t words2[2][8];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int chunk = (2 * (2 * wg + h) + c) ^ (r & 7);  // TMA 128-byte swizzle
-          const uint4 v = *reinterpret_cast<const uint4 *>(st + r * 128 + chunk * 16);
-          words2[h][4 * c + 0] = v.x; words2[h][4 * c + 1] = v.y; words2[h][4 * c + 2] = v.z; words2[h][4 * c + 3] = v.w;
+        if (have) {
+          sbits = __ldg(scales + (size_t)row * G + g);
+          bbits = __ldg(biases + (size_t)row * G + g);
         }
+      } else {
+        const int off = r * 16 + ((gs & 7) + wg) * 2;
+        sbits = *reinterpret_cast<const uint16_t *>(st + C::C_BYTES + off);
+        bbits = *reinterpret_cast<const uint16_t *>(st + C::C_BYTES + C::SB_BYTES + off);
+      }
+      // the group's 8 packed words of this row, then release the slot
+      uint32_t words[8];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int chunk = (2 * wg + c) ^ (r & 7);  // TMA 128-byte swizzle
+        const uint4 v = *reinterpret_cast<const uint4 *>(st + r * 128 + chunk * 16);
+        words[4 * c + 0] = v.x; words[4 * c + 1] = v.y; words[4 * c + 2] = v.z; words[4 * c + 3] = v.w;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&free_c[ring.slot]);
+      uint32_t a[32];
+      if (have) {
+        const __nv_bfloat162 s2 = u32_as_bf2(sbits | (sbits << 16));
+        const __nv_bfloat162 b2 = u32_as_bf2(bbits | (bbits << 16));
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int gl = 2 * wg + h;
-        const int gi = i * C::SG + gl;
-        if (ok && gs + gl < g1) {  // uniform across the warpgroup
-          const uint32_t(&words)[8] = words2[h];
-          const uint32_t sbits = h ? (s_pair >> 16) : (s_pair & 0xFFFFu);
-          const uint32_t bbits = h ? (b_pair >> 16) : (b_pair & 0xFFFFu);
-          const uint16_t nsb = float_to_bf16_bits(bf16_bits_to_float((uint16_t)sbits) * -128.f);  // exact
-          const __nv_bfloat162 s2 = u32_as_bf2(sbits | (sbits << 16));
-          const __nv_bfloat162 ns2 = u32_as_bf2(uint32_t(nsb) | (uint32_t(nsb) << 16));
-          uint32_t(&a)[32] = abuf[h];
-#pragma unroll
-          for (int wj = 0; wj < 8; ++wj) {
-            uint32_t o[4];
-            dequant_word_scaled(words[wj], s2, ns2, o);
-            a[4 * wj + 0] = o[0]; a[4 * wj + 1] = o[1]; a[4 * wj + 2] = o[2]; a[4 * wj + 3] = o[3];
-          }
-          // hand the previous group to the MMA, then make sure this slot is free
-          flush();
-          if (gi >= C::NAG && !warp_wait(&a_empty[aring.slot], aring.phase ^ 1u)) {
-            ok = false;
-          } else {
-            tc_fence_after();
-            const uint32_t bb = bbits | (bbits << 16);
-            const uint32_t bias_cols[8] = {bb, bb, bb, bb, bb, bb, bb, bb};
-            const uint32_t a_grp = lane_base + C::A_COL0 + aring.slot * C::GA;
-            tmem_st32(a_grp, a);
-            tmem_st8(a_grp + 32, bias_cols);
-            pend_slot = aring.slot;
-          }
+        for (int wj = 0; wj < 8; ++wj) {
+          uint32_t o[4];
+          dequant_word(words[wj], s2, b2, o);
+          a[4 * wj + 0] = o[0]; a[4 * wj + 1] = o[1]; a[4 * wj + 2] = o[2]; a[4 * wj + 3] = o[3];
         }
-        aring.next(C::NAG);
       }
-      aring.next(C::NAG);  // the other warpgroup's two groups
-      aring.next(C::NAG);
+      // the previous stage's store has drained behind this math: hand it over
+      flush();
+      // the stage slot is free once the MMAs of stage i - NAS have completed
+      if (i >= C::NAS && !warp_wait(&a_empty[aring.slot], aring.phase ^ 1u)) {
+        ok = false;
+        break;
+      }
+      if (have) {
+        tc_fence_after();
+        tmem_st32(lane_base + C::A_COL0 + (aring.slot * C::SG + wg) * C::GA, a);
+      }
+      pend = aring.slot;
     }
     flush();
     // ---------------- epilogue part 1: accumulator -> y or partials
     if (wg == 0 && ok && nst > 0 && warp_wait(acc_full, 0)) {
       tc_fence_after();
       float *red = reinterpret_cast<float *>(smem);  // [NP][128], the stage area is free now
+      // accumulator u holds data once some stage has a group in its range
+      int nacc = 1;
+      while (nacc < C::NI && g1 - g0 > nacc * (C::SG / C::NI)) ++nacc;
 #pragma unroll
       for (int c0 = 0; c0 < NP; c0 += 16) {
         uint32_t v[16];
         tmem_ld16(lane_base + c0, v);
         tmem_wait_ld();
+        for (int u = 1; u < nacc; ++u) {
+          uint32_t v1[16];
+          tmem_ld16(lane_base + u * NP + c0, v1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) + __uint_as_float(v1[e]));
+        }
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int t = c0 + e;
@@ -403,9 +409,8 @@ int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uin
   }
   const int tiles = N / 128;
   const int nst_all = (int)((G64 + C::SG - 1) / C::SG);
-  const int per_sm = NP <= 64 ? 2 : 1;  // resident CTAs per SM (TMEM and shared memory)
-  int splits = (per_sm * sm_count() + tiles / 2) / tiles;
-  if (splits < 1) splits = 1;
+  // one CTA per SM (all of TMEM): split K so that the grid fills the SMs in one wave
+  int splits = tiles >= sm_count() ? 1 : sm_count() / tiles;
   if (splits > 8) splits = 8;
   while (splits > 1 && nst_all / splits < 2) --splits;
   cudaLaunchConfig_t cfg = {};

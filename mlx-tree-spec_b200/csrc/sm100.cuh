@@ -55,6 +55,21 @@ TSB_HD bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps (issues nothing) until
+// the phase completes or about `hint_ns` elapse, so waiting warps leave the
+// issue slots to the warps that work.
+constexpr uint32_t kSuspendHintNs = 10u * 1000u * 1000u;
+TSB_HD bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 // Wait for the phase with the given parity to complete; false (and the device
 // status set to TSB_ETIMEOUT) if it does not within kWaitLimitNs, or if an
 // earlier wait anywhere has already failed.
@@ -62,8 +77,8 @@ TSB_HD bool mbar_wait(uint64_t *bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((it & 15u) == 0) {
       if (*(volatile unsigned int *)&g_device_status != 0u) return false;
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         record_status(TSB_ETIMEOUT);
