@@ -22,31 +22,31 @@
 //   warp 2    TMA producer of the x ring: x for the stage (four 64-K boxes of
 //             NP rows, 128-byte swizzle, rows >= M zero-filled by TMA); a slot
 //             is refilled when the MMAs that read it have completed.
-//   warps 1,3,5,7 MMA issuers (one lane each; two for NP = 128): per stage
-//             one wait, 4 (or 8) tcgen05.mma (M=128, N=NP, K=16) back to back
-//             and two commits; issuer u takes its share of each stage's groups
-//             into accumulator u (summed in the epilogue). A = the dequantized
+//   warps 1,3(,5) MMA issuers (one lane each, WGS of them): issuer u takes
+//             the stages i = u (mod WGS): one wait, 16 tcgen05.mma (M=128,
+//             N=NP, K=16) back to back and two commits per stage, into
+//             accumulator u (summed in the epilogue). A = the dequantized
 //             weights from TMEM, B = x from shared memory, f32 accumulators in
-//             TMEM. At N <= 64 an MMA costs ~27 ns whatever N is, so the issue
-//             loop carries no per-group synchronization.
-//   warps 8-23 dequantizers, four warpgroups; warpgroup w takes group w of
-//             every stage (thread = weight row = TMEM lane): codes ->
-//             bf16(s*q + b) -> tcgen05.st into a ring of stage slots in TMEM
-//             (4 groups each); a stage's store drains behind the next
-//             stage's arithmetic before it is handed to the MMA. One barrier
-//             pair per stage slot: all 16 dequantizer
-//             warps arrive on a_full, the MMA commits a_empty once per stage,
-//             and every waiter walks the stages in order, so no wait can run
-//             two phases ahead.
-//             Warpgroup 0 then runs the epilogue (TMEM -> registers -> bf16 y,
-//             or split-K partials).
+//             TMEM. Independent accumulators let the issuers' MMA streams
+//             overlap; per-stage waits and commits are paid once per stage.
+//   warps 8.. dequantizers, WGS warpgroups (3 for NP <= 32, else 2);
+//             warpgroup u owns the same stages as issuer u, all four groups of
+//             each (thread = weight row = TMEM lane): codes -> bf16(s*q + b) ->
+//             tcgen05.st into its own stage slot of A in TMEM, handed to issuer
+//             u once the stores have landed. Owning whole stages keeps the
+//             dequantizer warps of a sub-partition at different stages, so one
+//             warp's waits are covered by the others' arithmetic, and gives
+//             every ring slot and barrier a single waiter that walks its
+//             stages in order (no wait can run two phases ahead). Warpgroup 0
+//             then runs the epilogue (TMEM -> registers -> bf16 y, or split-K
+//             partials).
 //
 // Arithmetic: y = sum_k w_k x_k with w = bf16(fma(q, s, b)), the reference's
 // dequantization rule (qmm_packed.py:200, 348, 635) exactly: (code | 0x4300)
 // is bf16 128 + q, one bf16x2 subtract gives q exactly and one fused bf16x2
-// fma rounds q*s + b once. At N = NP <= 64 the MMA is bound by fetching its A
-// operand from TMEM (4 KB per instruction whatever N is), so the weights carry
-// the bias and each group costs only its four K=16 MMAs.
+// fma rounds q*s + b once. At N = NP <= 64 an M=128 K=16 MMA costs about the
+// same whatever N is (measured ~27 ns issued back to back), so the weights
+// carry the bias and each group costs only its four K=16 MMAs.
 #include "sm100.cuh"
 
 #include <cooperative_groups.h>
@@ -68,22 +68,25 @@ struct TsCfg {
   static constexpr int X_BOX_BYTES = NP * 128;     // one 64-K box of x
   static constexpr int XSLOT_BYTES = SG * X_BOX_BYTES;
   static constexpr int RING_BUDGET = 225 * 1024;   // shared memory for the two rings
-  static constexpr int NX = NP <= 32 ? 4 : (NP == 64 ? 3 : 2);                 // x slots
+  // WGS dequantizer warpgroups; warpgroup w owns the stages i = w (mod WGS)
+  // and A stage slot w. NI MMA issuers; issuer u takes part u (SG/NI groups)
+  // of every stage into accumulator u.
+  static constexpr int WGS = 3;
+  static constexpr int NI = NP <= 32 ? 4 : (NP <= 64 ? 2 : 1);  // MMA issuers, one accumulator each
+  static constexpr int GPI = SG / NI;              // groups per issuer part
+  static constexpr int NX = NP <= 32 ? 4 : (NP == 64 ? 3 : 2);  // x slots
   static constexpr int NC_FIT = (RING_BUDGET - NX * XSLOT_BYTES) / CSLOT_BYTES;
-  static constexpr int NC = NC_FIT > 12 ? 12 : NC_FIT;                        // codes slots
+  static constexpr int NC = (NC_FIT > 12 ? 12 : NC_FIT) / WGS * WGS;          // codes slots, a multiple of WGS
   static constexpr int X_AREA = NC * CSLOT_BYTES;
   static constexpr int STAGE_AREA = X_AREA + NX * XSLOT_BYTES;
-  static constexpr int NI = NP <= 64 ? 4 : 2;      // MMA issuers, one accumulator each
-  static constexpr int A_COL0 = NI * NP < 32 ? 32 : NI * NP;  // accumulators in [0, NI NP), A slots after
+  static constexpr int A_COL0 = (NI * NP + 31) / 32 * 32;  // accumulators in [0, NI NP), A slots after
   static constexpr int GA = 32;                    // per group slot: 64 bf16 weights per row
   static constexpr int TMEM_COLS = 512;
-  static constexpr int NAG_FIT = (TMEM_COLS - A_COL0) / GA;
-  static constexpr int NAS = (NAG_FIT > 12 ? 12 : NAG_FIT) / SG;  // stage slots of A in TMEM (4 groups each)
-  static constexpr int WGS = 4;                    // dequantizer warpgroups
+  static constexpr int NAS = WGS;                  // stage slots of A in TMEM (4 groups each), one per warpgroup
   static constexpr int DQ_WARP0 = 8;               // first dequantizer warp (lane quarter = warp & 3)
   static constexpr int THREADS = (DQ_WARP0 + 4 * WGS) * 32;
   static constexpr size_t SMEM = (size_t)STAGE_AREA + 1024 + 1024;
-  static_assert(NC >= 4 && NAS >= 2, "ring depths");
+  static_assert(NC >= WGS && A_COL0 + NAS * SG * GA <= TMEM_COLS, "ring depths and TMEM columns");
   static_assert(CSLOT_BYTES % 1024 == 0 && XSLOT_BYTES % 1024 == 0, "slot alignment (128-byte swizzle atoms)");
   static_assert(NP * 512 <= STAGE_AREA, "split-K partials fit in the stage area");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
@@ -114,7 +117,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   uint64_t *full_x = bars + 2 * C::NC;           // [NX] x landed
   uint64_t *free_x = full_x + C::NX;             // [NX] MMAs that read the slot are done
   uint64_t *a_full = free_x + C::NX;             // [NAS] stage written into TMEM
-  uint64_t *a_empty = a_full + C::NAS;           // [NAS] MMA done with the stage slot
+  uint64_t *a_empty = a_full + C::NAS;           // [NAS] MMAs done with the stage slot
   uint64_t *acc_full = a_empty + C::NAS;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
 
@@ -136,15 +139,15 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NC; ++s) {
       mbar_init(&full_c[s], 1);
-      mbar_init(&free_c[s], 16);  // every dequantizer warp
+      mbar_init(&free_c[s], 4);  // the 4 warps of the stage's warpgroup
     }
     for (int s = 0; s < C::NX; ++s) {
       mbar_init(&full_x[s], 1);
       mbar_init(&free_x[s], C::NI);  // every MMA issuer
     }
     for (int b = 0; b < C::NAS; ++b) {
-      mbar_init(&a_full[b], 16);  // every dequantizer warp
-      mbar_init(&a_empty[b], C::NI);
+      mbar_init(&a_full[b], 4);      // the 4 warps of the owning warpgroup
+      mbar_init(&a_empty[b], C::NI);  // every MMA issuer
     }
     mbar_init(acc_full, C::NI);
     fence_mbar_init();
@@ -209,27 +212,25 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       }
     }
   } else if ((warp & 1) && warp < 2 * C::NI) {
-    // ---------------- MMA issuers: warp 2u+1 takes groups [u, u+1) * SG/NI of
-    // every stage into accumulator u (independent MMA streams keep the tensor
-    // pipe busier than one dependent chain); one lane each, descriptors built
-    // once per stage and advanced by adding the 16-byte-unit offset of each
-    // 64-K box and 16-K slice
+    // ---------------- MMA issuers: warp 2u+1 takes part u of every stage into
+    // accumulator u; one lane each, descriptors built once per stage and
+    // advanced by adding the 16-byte-unit offset of each 64-K box and 16-K slice
     const int u = warp >> 1;
-    constexpr int GPI = C::SG / C::NI;  // groups per issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, NP);
       const uint32_t dacc = tmem_base + (uint32_t)(u * NP);
       bool ok = true, first = true;
       Ring ring, aring;
       for (int i = 0; i < nst && ok; ++i, ring.next(C::NX), aring.next(C::NAS)) {
-        ok = mbar_wait(&full_x[ring.slot], ring.phase) && mbar_wait(&a_full[aring.slot], aring.phase);
+        ok = mbar_wait(&full_x[ring.slot], ring.phase) &&
+             mbar_wait(&a_full[aring.slot], aring.phase);
         if (!ok) break;
         tc_fence_after();
         const int gs = g0 + i * C::SG;
-        const int gend = min(GPI * (u + 1), g1 - gs);
+        const int gend = min(C::GPI * (u + 1), g1 - gs);
         const uint64_t xd = desc_kmajor_sw128(smem_addr(xslot(ring.slot)));
-        const uint32_t a0 = tmem_base + C::A_COL0 + aring.slot * C::SG * C::GA;
-        for (int gl = GPI * u; gl < gend; ++gl) {
+        const uint32_t a0 = tmem_base + C::A_COL0 + (uint32_t)(aring.slot * C::SG * C::GA);
+        for (int gl = C::GPI * u; gl < gend; ++gl) {
           const uint32_t ag = a0 + gl * C::GA;
           const uint64_t bd = xd + (uint64_t)((gl * C::X_BOX_BYTES) >> 4);
           mma_ts_f16(dacc, ag, bd, idesc, first ? 0u : 1u);
@@ -240,90 +241,97 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         }
         mma_commit(&a_empty[aring.slot]);
         mma_commit(&free_x[ring.slot]);
-        if (i == nst - 1) mma_commit(acc_full);
       }
+      mma_commit(acc_full);  // every issuer arrives once, with or without groups
     }
     __syncwarp();
   } else if (warp >= C::DQ_WARP0) {
     // ---------------- dequantizers (thread = weight row = TMEM lane)
     const int q = warp & 3;
-    const int wg = (warp - C::DQ_WARP0) >> 2;  // group wg of every stage
+    const int wg = (warp - C::DQ_WARP0) >> 2;  // owns stages i = wg (mod WGS)
     const int r = q * 32 + lane;
     const int row = n0 + r;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     bool ok = true;
-    int pend = -1;  // stage slot whose TMEM store is still draining
-    auto flush = [&]() {
-      if (pend >= 0) {
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&a_full[pend]);
-        pend = -1;
-      }
-    };
-    Ring ring, aring;
-    for (int i = 0; i < nst && ok; ++i, ring.next(C::NC), aring.next(C::NAS)) {
-      ok = warp_wait(&full_c[ring.slot], ring.phase);
+    // Stage i lives in codes slot i % NC (NC % WGS == 0) and A stage slot
+    // i % WGS = wg: every slot and every barrier has one owning warpgroup,
+    // which walks its stages in order, so no wait can run two phases ahead.
+    int cs = wg;
+    uint32_t cphase = 0;
+    int ai = 0;  // this warpgroup's stage count: phase of its A slot
+    uint32_t a[32];
+    for (int i = wg; i < nst && ok; i += C::WGS) {
+      ok = warp_wait(&full_c[cs], cphase);
       if (!ok) break;
       const int gs = g0 + i * C::SG;
-      const int g = gs + wg;
-      const bool have = g < g1;  // uniform across the warpgroup
-      const unsigned char *st = cslot(ring.slot);
-      // this row's scale and bias of the group
-      uint32_t sbits = 0, bbits = 0;
+      const int ng = min(C::SG, g1 - gs);  // uniform
+      const unsigned char *st = cslot(cs);
+      // this row's scales and biases of the stage's four groups (8-byte loads)
+      uint32_t s_w[2], b_w[2];
       if (sb_direct) {
-        if (have) {
-          sbits = __ldg(scales + (size_t)row * G + g);
-          bbits = __ldg(biases + (size_t)row * G + g);
+#pragma unroll
+        for (int hw = 0; hw < 2; ++hw) {
+          const int ga = gs + 2 * hw;
+          const size_t idx = (size_t)row * G + ga;
+          const bool v0 = ga < g1, v1 = ga + 1 < g1;
+          s_w[hw] = (v0 ? uint32_t(__ldg(scales + idx)) : 0u) | (v1 ? uint32_t(__ldg(scales + idx + 1)) << 16 : 0u);
+          b_w[hw] = (v0 ? uint32_t(__ldg(biases + idx)) : 0u) | (v1 ? uint32_t(__ldg(biases + idx + 1)) << 16 : 0u);
         }
       } else {
-        const int off = r * 16 + ((gs & 7) + wg) * 2;
-        sbits = *reinterpret_cast<const uint16_t *>(st + C::C_BYTES + off);
-        bbits = *reinterpret_cast<const uint16_t *>(st + C::C_BYTES + C::SB_BYTES + off);
+        const int off = r * 16 + (gs & 7) * 2;  // (gs & 7) is 0 or 4: 8-byte aligned
+        const uint2 sv = *reinterpret_cast<const uint2 *>(st + C::C_BYTES + off);
+        const uint2 bv = *reinterpret_cast<const uint2 *>(st + C::C_BYTES + C::SB_BYTES + off);
+        s_w[0] = sv.x; s_w[1] = sv.y; b_w[0] = bv.x; b_w[1] = bv.y;
       }
-      // the group's 8 packed words of this row, then release the slot
-      uint32_t words[8];
+      // the stage's 32 packed words of this row, then release the codes slot
+      uint32_t words[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int chunk = (2 * wg + c) ^ (r & 7);  // TMA 128-byte swizzle
+      for (int c = 0; c < 8; ++c) {
+        const int chunk = c ^ (r & 7);  // TMA 128-byte swizzle
         const uint4 v = *reinterpret_cast<const uint4 *>(st + r * 128 + chunk * 16);
         words[4 * c + 0] = v.x; words[4 * c + 1] = v.y; words[4 * c + 2] = v.z; words[4 * c + 3] = v.w;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&free_c[ring.slot]);
-      uint32_t a[32];
-      if (have) {
-        const __nv_bfloat162 s2 = u32_as_bf2(sbits | (sbits << 16));
-        const __nv_bfloat162 b2 = u32_as_bf2(bbits | (bbits << 16));
-#pragma unroll
-        for (int wj = 0; wj < 8; ++wj) {
-          uint32_t o[4];
-          dequant_word(words[wj], s2, b2, o);
-          a[4 * wj + 0] = o[0]; a[4 * wj + 1] = o[1]; a[4 * wj + 2] = o[2]; a[4 * wj + 3] = o[3];
-        }
-      }
-      // the previous stage's store has drained behind this math: hand it over
-      flush();
-      // the stage slot is free once the MMAs of stage i - NAS have completed
-      if (i >= C::NAS && !warp_wait(&a_empty[aring.slot], aring.phase ^ 1u)) {
+      if (lane == 0) mbar_arrive(&free_c[cs]);
+      // the A slot is free once the MMAs of this warpgroup's previous stage completed
+      if (ai > 0 && !warp_wait(&a_empty[wg], (uint32_t)((ai - 1) & 1))) {
         ok = false;
         break;
       }
-      if (have) {
-        tc_fence_after();
-        tmem_st32(lane_base + C::A_COL0 + (aring.slot * C::SG + wg) * C::GA, a);
+      tc_fence_after();
+#pragma unroll
+      for (int gl = 0; gl < C::SG; ++gl) {
+        if (gl >= ng) break;
+        const uint32_t sb = (s_w[gl >> 1] >> (16 * (gl & 1))) & 0xFFFFu;
+        const uint32_t bb = (b_w[gl >> 1] >> (16 * (gl & 1))) & 0xFFFFu;
+        const __nv_bfloat162 s2 = u32_as_bf2(sb | (sb << 16));
+        const __nv_bfloat162 b2 = u32_as_bf2(bb | (bb << 16));
+#pragma unroll
+        for (int wj = 0; wj < 8; ++wj) {
+          uint32_t o[4];
+          dequant_word(words[gl * 8 + wj], s2, b2, o);
+          a[4 * wj + 0] = o[0]; a[4 * wj + 1] = o[1]; a[4 * wj + 2] = o[2]; a[4 * wj + 3] = o[3];
+        }
+        tmem_st32(lane_base + C::A_COL0 + (wg * C::SG + gl) * C::GA, a);
       }
-      pend = aring.slot;
+      // tcgen05.st reads its source registers at issue (a is reused above); the
+      // stores must only have reached TMEM before the issuers are told
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[wg]);
+      if (!ok) break;
+      ++ai;
+      cs += C::WGS;
+      if (cs >= C::NC) { cs -= C::NC; cphase ^= 1u; }
     }
-    flush();
     // ---------------- epilogue part 1: accumulator -> y or partials
     if (wg == 0 && ok && nst > 0 && warp_wait(acc_full, 0)) {
       tc_fence_after();
       float *red = reinterpret_cast<float *>(smem);  // [NP][128], the stage area is free now
-      // accumulator u holds data once some stage has a group in its range
+      // accumulator u holds data once some stage has a group in its part
       int nacc = 1;
-      while (nacc < C::NI && g1 - g0 > nacc * (C::SG / C::NI)) ++nacc;
+      while (nacc < C::NI && g1 - g0 > nacc * C::GPI) ++nacc;
 #pragma unroll
       for (int c0 = 0; c0 < NP; c0 += 16) {
         uint32_t v[16];
