@@ -379,6 +379,9 @@ def run_tsb(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved_gbs / hbm_peak, 4), "traffic": traffic,
                          "kernel": "qmm_ts_kernel", "peak_source": peak_src,
+                         "traffic_basis": "dram read+write bytes per step (15 launches) from one ncu capture "
+                                          "(profiles/qmm_verify_sweep_traffic.txt); algorithmic bytes per step "
+                                          f"{total_bytes}",
                          "basis": "sum of algorithmic bytes / sum of per-call device time over the 15 calls"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
@@ -397,7 +400,7 @@ def run_tsb(args):
 
 def read_traffic():
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "qmm_small_sweep_traffic.txt")
+    p = os.path.join(ROOT, "profiles", "qmm_verify_sweep_traffic.txt")
     try:
         for ln in open(p):
             if ln.startswith("traffic_bytes_per_step:"):
