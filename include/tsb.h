@@ -83,6 +83,14 @@ int tsb_device_status(tsb_stream_t stream, int reset);
  * Requirements: M >= 1, N % 128 == 0, K % 64 == 0, ldy % 8 == 0; x, w, y
  * 16-byte aligned. Accumulation in float32. Declines (TSB_EUNSUPPORTED)
  * other N/K granularities.
+ *
+ * Workspace (M <= 128, the verify path): tsb_qmm_workspace_bytes(M, N, K)
+ * bytes, 256-byte aligned, computed for the current device. It holds
+ * completion flags and float partials of row tiles shared between CTAs. It
+ * must be zero-filled once before its first use (cudaMemset); every call
+ * leaves it zero again. Do not share it with other work or with calls in
+ * flight on another stream. Too small or NULL: TSB_EWORKSPACE. M > 128 (the
+ * prefill GEMM) needs none (size 0).
  * ---------------------------------------------------------------------- */
 size_t tsb_qmm_workspace_bytes(int M, int N, int K);
 int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const void *biases, void *y,

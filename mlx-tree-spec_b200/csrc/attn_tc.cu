@@ -292,6 +292,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       }
       tmem_wait_st();
       tc_fence_before();
+      fence_proxy_async_smem();  // the staging slots are refilled by TMA (async proxy)
       __syncwarp();
       if (lane == 0) mbar_arrive(q_done);
     }

@@ -5,7 +5,8 @@
 
 namespace tsb {
 int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-           int K, int ldy, cudaStream_t st);
+           int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t qmm_ts_workspace_bytes(int M, int N, int K);
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
              int K, int ldy, cudaStream_t st);
 
@@ -17,11 +18,11 @@ constexpr int kTsMaxRows = 128;
 
 using namespace tsb;
 
+// The verify path (M <= 128) needs completion flags and the float partials of
+// the row tiles it splits across CTAs; the prefill GEMM needs nothing.
 extern "C" size_t tsb_qmm_workspace_bytes(int M, int N, int K) {
-  (void)N;
-  (void)M;
-  (void)K;
-  return 0;  // neither path needs scratch memory
+  if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 64) return 0;
+  return M <= kTsMaxRows ? qmm_ts_workspace_bytes(M, N, K) : 0;
 }
 
 extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const void *biases, void *y,
@@ -31,11 +32,9 @@ extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scale
   if (K % 64 || N % 128) return TSB_EUNSUPPORTED;
   if (ldy % 8) return TSB_EINVAL;
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16)) return TSB_EINVAL;
-  (void)ws;
-  (void)ws_bytes;
   if (M <= kTsMaxRows)
     return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
-                  ldy, (cudaStream_t)stream);
+                  ldy, ws, ws_bytes, (cudaStream_t)stream);
   return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
                   ldy, (cudaStream_t)stream);
 }

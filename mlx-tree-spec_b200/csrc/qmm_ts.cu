@@ -11,48 +11,53 @@
 // 4 bytes of shared-memory traffic per weight; tcgen05.st into TMEM keeps the
 // shared-memory path for the packed codes and x only.
 //
-// CTA: 128 weight rows (one TMEM lane each) x all tokens (NP = M rounded up
-// to 16), a K range of whole stages (4 groups = 256 K each); one CTA per SM
-// (all 512 TMEM columns); split-K CTAs of one row tile form a cluster and
-// reduce through distributed shared memory. Warp roles:
-//   warp 0    TMA producer of the codes ring: per stage the codes of the 128
-//             rows (32 words each, 128-byte swizzle) and their scales and
-//             biases (8-group boxes). A slot is refilled as soon as its
-//             dequantizers have loaded its words into registers.
-//   warp 2    TMA producer of the x ring: x for the stage (four 64-K boxes of
-//             NP rows, 128-byte swizzle, rows >= M zero-filled by TMA); a slot
-//             is refilled when the MMAs that read it have completed.
-//   warps 1,3(,5) MMA issuers (one lane each, WGS of them): issuer u takes
-//             the stages i = u (mod WGS): one wait, 16 tcgen05.mma (M=128,
-//             N=NP, K=16) back to back and two commits per stage, into
-//             accumulator u (summed in the epilogue). A = the dequantized
-//             weights from TMEM, B = x from shared memory, f32 accumulators in
-//             TMEM. Independent accumulators let the issuers' MMA streams
-//             overlap; per-stage waits and commits are paid once per stage.
-//   warps 8.. dequantizers, WGS warpgroups (3 for NP <= 32, else 2);
-//             warpgroup u owns the same stages as issuer u, all four groups of
-//             each (thread = weight row = TMEM lane): codes -> bf16(s*q + b) ->
-//             tcgen05.st into its own stage slot of A in TMEM, handed to issuer
-//             u once the stores have landed. Owning whole stages keeps the
-//             dequantizer warps of a sub-partition at different stages, so one
-//             warp's waits are covered by the others' arithmetic, and gives
-//             every ring slot and barrier a single waiter that walks its
-//             stages in order (no wait can run two phases ahead). Warpgroup 0
-//             then runs the epilogue (TMEM -> registers -> bf16 y, or split-K
-//             partials).
+// Schedule: a persistent, stream-K grid of P <= #SM co-resident CTAs (one per
+// SM: all 512 TMEM columns). The work is the list of (row tile of 128 weight
+// rows, stage of 4 groups = 256 K) units, tile-major; CTA c takes the
+// contiguous units [U c / P, U (c+1) / P). Its range crosses tile boundaries,
+// so it works on a sequence of tile segments. A segment that covers a whole
+// tile writes y directly. A tile split over CTAs c_lo < ... < c_hi: the parts
+// of c_lo+1..c_hi (which end early in those CTAs' ranges) go to the workspace
+// as float partials with a completion flag each; c_lo, whose part is the last
+// segment of its range, waits for the flags, adds the partials, writes y and
+// clears the flags (the workspace is left as it was found: flags zero).
+//
+// Warp roles (thread = weight row = TMEM lane wherever TMEM is touched):
+//   warps 0-3  epilogue: per segment, accumulators -> registers -> y, partial
+//              or fixup; warp 0 also allocates TMEM.
+//   warp 4     TMA producer of the codes ring: per stage the codes of the 128
+//              rows (32 words each, 128-byte swizzle) and their scales and
+//              biases (8-group boxes). A slot is refilled as soon as its
+//              dequantizers have loaded its words into registers.
+//   warp 5     TMA producer of the x ring: x for the stage (four 64-K boxes of
+//              NP rows, 128-byte swizzle, rows >= M zero-filled by TMA); a slot
+//              is refilled when the MMAs that read it have completed.
+//   warps 6,7,20,21  MMA issuers (NI of them, one lane each): issuer u takes
+//              its share of every stage's groups into accumulator u (summed in
+//              the epilogue); per stage one wait, the MMAs back to back and two
+//              commits. A = the dequantized weights from TMEM, B = x from
+//              shared memory, f32 accumulators in TMEM. At N <= 64 an M=128
+//              K=16 MMA costs about the same whatever N is (~27 ns issued back
+//              to back), so independent accumulators from several issuers keep
+//              the tensor pipe busier than one dependent chain.
+//   warps 8-19 dequantizers, three warpgroups: warpgroup w owns the stages
+//              i = w (mod 3) of the CTA's range, all four groups of each:
+//              codes -> bf16(s*q + b) -> tcgen05.st into its own stage slot of
+//              A in TMEM, handed to the issuers once the stores have landed.
+//              Owning whole stages keeps the dequantizer warps of a
+//              sub-partition at different stages (one warp's waits are covered
+//              by the others' arithmetic).
+// Every ring slot and every mbarrier has waiters that walk their stages (or
+// segments) in order, so no parity wait can run two phases ahead.
 //
 // Arithmetic: y = sum_k w_k x_k with w = bf16(fma(q, s, b)), the reference's
 // dequantization rule (qmm_packed.py:200, 348, 635) exactly: (code | 0x4300)
 // is bf16 128 + q, one bf16x2 subtract gives q exactly and one fused bf16x2
-// fma rounds q*s + b once. At N = NP <= 64 an M=128 K=16 MMA costs about the
-// same whatever N is (measured ~27 ns issued back to back), so the weights
-// carry the bias and each group costs only its four K=16 MMAs.
+// fma rounds q*s + b once. The weights carry the bias, so each group costs
+// only its four K=16 MMAs.
 #include "sm100.cuh"
 
-#include <cooperative_groups.h>
 #include <string.h>
-
-namespace cg = cooperative_groups;
 
 namespace tsb {
 
@@ -68,27 +73,22 @@ struct TsCfg {
   static constexpr int X_BOX_BYTES = NP * 128;     // one 64-K box of x
   static constexpr int XSLOT_BYTES = SG * X_BOX_BYTES;
   static constexpr int RING_BUDGET = 225 * 1024;   // shared memory for the two rings
-  // WGS dequantizer warpgroups; warpgroup w owns the stages i = w (mod WGS)
-  // and A stage slot w. NI MMA issuers; issuer u takes part u (SG/NI groups)
-  // of every stage into accumulator u.
-  static constexpr int WGS = 3;
+  static constexpr int WGS = 3;                    // dequantizer warpgroups = A stage slots
   static constexpr int NI = NP <= 32 ? 4 : (NP <= 64 ? 2 : 1);  // MMA issuers, one accumulator each
-  static constexpr int GPI = SG / NI;              // groups per issuer part
+  static constexpr int GPI = SG / NI;              // groups per issuer
   static constexpr int NX = NP <= 32 ? 4 : (NP == 64 ? 3 : 2);  // x slots
   static constexpr int NC_FIT = (RING_BUDGET - NX * XSLOT_BYTES) / CSLOT_BYTES;
-  static constexpr int NC = (NC_FIT > 12 ? 12 : NC_FIT) / WGS * WGS;          // codes slots, a multiple of WGS
+  static constexpr int NC = (NC_FIT > 12 ? 12 : NC_FIT) / WGS * WGS;  // codes slots, a multiple of WGS
   static constexpr int X_AREA = NC * CSLOT_BYTES;
   static constexpr int STAGE_AREA = X_AREA + NX * XSLOT_BYTES;
   static constexpr int A_COL0 = (NI * NP + 31) / 32 * 32;  // accumulators in [0, NI NP), A slots after
-  static constexpr int GA = 32;                    // per group slot: 64 bf16 weights per row
+  static constexpr int GA = 32;                    // per group: 64 bf16 weights per row
   static constexpr int TMEM_COLS = 512;
-  static constexpr int NAS = WGS;                  // stage slots of A in TMEM (4 groups each), one per warpgroup
-  static constexpr int DQ_WARP0 = 8;               // first dequantizer warp (lane quarter = warp & 3)
-  static constexpr int THREADS = (DQ_WARP0 + 4 * WGS) * 32;
+  static constexpr int CODES_WARP = 4, X_WARP = 5, DQ_WARP0 = 8;  // epilogue: warps 0-3
+  static constexpr int THREADS = (NI > 2 ? 22 : 20) * 32;
   static constexpr size_t SMEM = (size_t)STAGE_AREA + 1024 + 1024;
-  static_assert(NC >= WGS && A_COL0 + NAS * SG * GA <= TMEM_COLS, "ring depths and TMEM columns");
+  static_assert(NC >= WGS && A_COL0 + WGS * SG * GA <= TMEM_COLS, "ring depths and TMEM columns");
   static_assert(CSLOT_BYTES % 1024 == 0 && XSLOT_BYTES % 1024 == 0, "slot alignment (128-byte swizzle atoms)");
-  static_assert(NP * 512 <= STAGE_AREA, "split-K partials fit in the stage area");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -101,12 +101,44 @@ struct Ring {
   }
 };
 
+// Stream-K partition: CTA c of P owns units [U c / P, U (c+1) / P). The owners
+// of tile t (units [t nst, (t+1) nst)) are CTAs c_lo(t) .. c_hi(t).
+struct Part {
+  long long U;
+  int P, nst;
+  TSB_HD long long start(int c) const { return U * c / P; }
+  TSB_HD int c_lo(int t) const {
+    const long long a = (long long)t * nst;
+    return (int)(((a + 1) * P + U - 1) / U) - 1;
+  }
+  TSB_HD int c_hi(int t) const {
+    const long long b = (long long)(t + 1) * nst;
+    return (int)((b * P + U - 1) / U) - 1;
+  }
+};
+
+struct TsArgs {
+  const uint16_t *scales, *biases;
+  uint16_t *y;
+  float *partials;     // [tiles][maxp][NP][128], part 0 unused
+  uint32_t *flags;     // [tiles][maxp], zero between calls
+  long long U;
+  int M, N, K, ldy, P, nst, maxp;
+};
+
+TSB_HD uint32_t ld_acquire_gpu(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+TSB_HD void st_release_gpu(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 template <int NP>
 __global__ void __launch_bounds__(TsCfg<NP>::THREADS, 1)
 qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-              const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b,
-              const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases,
-              uint16_t *__restrict__ y, int M, int N, int K, int ldy, int splits) {
+              const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b, TsArgs a) {
   using C = TsCfg<NP>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
@@ -116,25 +148,32 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   uint64_t *free_c = bars + C::NC;               // [NC] dequantizers have loaded the slot
   uint64_t *full_x = bars + 2 * C::NC;           // [NX] x landed
   uint64_t *free_x = full_x + C::NX;             // [NX] MMAs that read the slot are done
-  uint64_t *a_full = free_x + C::NX;             // [NAS] stage written into TMEM
-  uint64_t *a_empty = a_full + C::NAS;           // [NAS] MMAs done with the stage slot
-  uint64_t *acc_full = a_empty + C::NAS;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+  uint64_t *a_full = free_x + C::NX;             // [WGS] stage written into TMEM
+  uint64_t *a_empty = a_full + C::WGS;           // [WGS] MMAs done with the stage slot
+  uint64_t *acc_full = a_empty + C::WGS;         // segment accumulated
+  uint64_t *acc_empty = acc_full + 1;            // accumulators read by the epilogue
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int n0 = blockIdx.x * C::ROWS;
-  const int split = blockIdx.y;
-  const int G = K / 64;
-  const int nst_all = (G + C::SG - 1) / C::SG;
-  const int st0 = (int)((long long)split * nst_all / splits);
-  const int st1 = (int)((long long)(split + 1) * nst_all / splits);
-  const int nst = st1 - st0;
-  const int g0 = st0 * C::SG;
-  const int g1 = min(G, st1 * C::SG);
+  const Part part{a.U, a.P, a.nst};
+  const int c = blockIdx.x;
+  const long long u0 = part.start(c);
+  const int L = (int)(part.start(c + 1) - u0);  // stages of this CTA
+  const int G = a.K / 64;
   // G % 8 != 0: the scale rows' pitch (2G bytes) is not a multiple of 16, which
   // TMA tiles require; the dequantizers then load their row's scales and
   // biases directly (odd shapes only; model shapes have K % 512 == 0).
   const bool sb_direct = (G % 8) != 0;
+  // (tile, stage within the tile) of local stage li; loops advance it with step()
+  auto unit = [&](int li, int &tile, int &st) {
+    const long long u = u0 + li;
+    tile = (int)(u / a.nst);
+    st = (int)(u - (long long)tile * a.nst);
+  };
+  auto step = [&](int &tile, int &st, int by) {
+    st += by;
+    while (st >= a.nst) { st -= a.nst; ++tile; }
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NC; ++s) {
@@ -145,11 +184,12 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       mbar_init(&full_x[s], 1);
       mbar_init(&free_x[s], C::NI);  // every MMA issuer
     }
-    for (int b = 0; b < C::NAS; ++b) {
+    for (int b = 0; b < C::WGS; ++b) {
       mbar_init(&a_full[b], 4);      // the 4 warps of the owning warpgroup
       mbar_init(&a_empty[b], C::NI);  // every MMA issuer
     }
     mbar_init(acc_full, C::NI);
+    mbar_init(acc_empty, 4);  // the epilogue warps
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -164,9 +204,9 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   auto cslot = [&](int s) { return smem + (size_t)s * C::CSLOT_BYTES; };
   auto xslot = [&](int s) { return smem + C::X_AREA + (size_t)s * C::XSLOT_BYTES; };
 
-  if (warp == 0 || warp == 2) {
-    // ---------------- TMA producers: warp 0 the codes ring, warp 2 the x ring
-    const bool codes = warp == 0;
+  if (warp == C::CODES_WARP || warp == C::X_WARP) {
+    // ---------------- TMA producers
+    const bool codes = warp == C::CODES_WARP;
     const int nslots = codes ? C::NC : C::NX;
     uint64_t *full = codes ? full_c : full_x;
     uint64_t *freed = codes ? free_c : free_x;
@@ -182,17 +222,20 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       }
       Ring ring;
       int issued = 0;
-      for (int i = 0; i < nst; ++i, ring.next(nslots)) {
-        if (i >= nslots && !mbar_wait(&freed[ring.slot], ring.phase ^ 1u)) break;
-        const int gs = g0 + i * C::SG;
+      int tile, st;
+      unit(0, tile, st);
+      for (int li = 0; li < L; ++li, ring.next(nslots), step(tile, st, 1)) {
+        if (li >= nslots && !mbar_wait(&freed[ring.slot], ring.phase ^ 1u)) break;
+        const int gs = st * C::SG;
         if (codes) {
-          unsigned char *st = cslot(ring.slot);
+          unsigned char *cs = cslot(ring.slot);
+          const int n0 = tile * C::ROWS;
           mbar_arrive_expect_tx(&full[ring.slot], C::C_BYTES + (sb_direct ? 0 : 2 * C::SB_BYTES));
-          tma_load_2d(st, &tmap_w, gs * 8, n0, &full[ring.slot]);
+          tma_load_2d(cs, &tmap_w, gs * 8, n0, &full[ring.slot]);
           if (!sb_direct) {
             const int gb = gs & ~7;  // 8-group box containing this stage's groups
-            tma_load_2d(st + C::C_BYTES, &tmap_s, gb, n0, &full[ring.slot]);
-            tma_load_2d(st + C::C_BYTES + C::SB_BYTES, &tmap_b, gb, n0, &full[ring.slot]);
+            tma_load_2d(cs + C::C_BYTES, &tmap_s, gb, n0, &full[ring.slot]);
+            tma_load_2d(cs + C::C_BYTES + C::SB_BYTES, &tmap_b, gb, n0, &full[ring.slot]);
           }
         } else {
           unsigned char *xt = xslot(ring.slot);
@@ -201,7 +244,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
           for (int gl = 0; gl < C::SG; ++gl)
             tma_load_2d(xt + gl * C::X_BOX_BYTES, &tmap_x, (gs + gl) * 64, 0, &full[ring.slot]);
         }
-        issued = i + 1;
+        issued = li + 1;
       }
       // drain: every issued load has landed before the CTA can exit
       for (int i = (issued > nslots ? issued - nslots : 0); i < issued; ++i) {
@@ -211,23 +254,32 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         }
       }
     }
-  } else if ((warp & 1) && warp < 2 * C::NI) {
-    // ---------------- MMA issuers: warp 2u+1 takes part u of every stage into
-    // accumulator u; one lane each, descriptors built once per stage and
-    // advanced by adding the 16-byte-unit offset of each 64-K box and 16-K slice
-    const int u = warp >> 1;
+  } else if ((warp == 6 || warp == 7 || warp == 20 || warp == 21) &&
+             (warp < 20 ? warp - 6 : warp - 18) < C::NI) {
+    // ---------------- MMA issuers: issuer u takes groups [u, u+1) * GPI of every
+    // stage into accumulator u; one lane each, descriptors built once per stage
+    // and advanced by adding the 16-byte-unit offset of each 64-K box and 16-K slice
+    const int u = warp < 20 ? warp - 6 : warp - 18;
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, NP);
       const uint32_t dacc = tmem_base + (uint32_t)(u * NP);
       bool ok = true, first = true;
+      int seg = 0;
       Ring ring, aring;
-      for (int i = 0; i < nst && ok; ++i, ring.next(C::NX), aring.next(C::NAS)) {
-        ok = mbar_wait(&full_x[ring.slot], ring.phase) &&
-             mbar_wait(&a_full[aring.slot], aring.phase);
+      int tile, st;
+      unit(0, tile, st);
+      for (int li = 0; li < L && ok; ++li, ring.next(C::NX), aring.next(C::WGS), step(tile, st, 1)) {
+        if (li > 0 && st == 0) {
+          // a new segment: the epilogue must have read the accumulators
+          ok = mbar_wait(acc_empty, (uint32_t)((seg - 1) & 1));
+          if (!ok) break;
+          first = true;
+        }
+        ok = mbar_wait(&full_x[ring.slot], ring.phase) && mbar_wait(&a_full[aring.slot], aring.phase);
         if (!ok) break;
         tc_fence_after();
-        const int gs = g0 + i * C::SG;
-        const int gend = min(C::GPI * (u + 1), g1 - gs);
+        const int gs = st * C::SG;
+        const int gend = min(C::GPI * (u + 1), G - gs);
         const uint64_t xd = desc_kmajor_sw128(smem_addr(xslot(ring.slot)));
         const uint32_t a0 = tmem_base + C::A_COL0 + (uint32_t)(aring.slot * C::SG * C::GA);
         for (int gl = C::GPI * u; gl < gend; ++gl) {
@@ -241,31 +293,35 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         }
         mma_commit(&a_empty[aring.slot]);
         mma_commit(&free_x[ring.slot]);
+        if (li == L - 1 || st == a.nst - 1) {  // the segment's last stage
+          mma_commit(acc_full);
+          ++seg;
+        }
       }
-      mma_commit(acc_full);  // every issuer arrives once, with or without groups
     }
     __syncwarp();
-  } else if (warp >= C::DQ_WARP0) {
+  } else if (warp >= C::DQ_WARP0 && warp < C::DQ_WARP0 + 4 * C::WGS) {
     // ---------------- dequantizers (thread = weight row = TMEM lane)
     const int q = warp & 3;
-    const int wg = (warp - C::DQ_WARP0) >> 2;  // owns stages i = wg (mod WGS)
+    const int wg = (warp - C::DQ_WARP0) >> 2;  // owns local stages li = wg (mod WGS)
     const int r = q * 32 + lane;
-    const int row = n0 + r;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     bool ok = true;
-    // Stage i lives in codes slot i % NC (NC % WGS == 0) and A stage slot
-    // i % WGS = wg: every slot and every barrier has one owning warpgroup,
-    // which walks its stages in order, so no wait can run two phases ahead.
+    // Stage li lives in codes slot li % NC (NC % WGS == 0) and A stage slot
+    // li % WGS = wg, so this warpgroup is the only waiter of its slots.
     int cs = wg;
     uint32_t cphase = 0;
     int ai = 0;  // this warpgroup's stage count: phase of its A slot
-    uint32_t a[32];
-    for (int i = wg; i < nst && ok; i += C::WGS) {
+    uint32_t wt[32];  // one group's 64 dequantized weights (bf16 pairs)
+    int tile, st;
+    unit(wg, tile, st);
+    for (int li = wg; li < L && ok; li += C::WGS, step(tile, st, C::WGS)) {
       ok = warp_wait(&full_c[cs], cphase);
       if (!ok) break;
-      const int gs = g0 + i * C::SG;
-      const int ng = min(C::SG, g1 - gs);  // uniform
-      const unsigned char *st = cslot(cs);
+      const int row = tile * C::ROWS + r;
+      const int gs = st * C::SG;
+      const int ng = min(C::SG, G - gs);  // uniform
+      const unsigned char *cb = cslot(cs);
       // this row's scales and biases of the stage's four groups (8-byte loads)
       uint32_t s_w[2], b_w[2];
       if (sb_direct) {
@@ -273,24 +329,29 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         for (int hw = 0; hw < 2; ++hw) {
           const int ga = gs + 2 * hw;
           const size_t idx = (size_t)row * G + ga;
-          const bool v0 = ga < g1, v1 = ga + 1 < g1;
-          s_w[hw] = (v0 ? uint32_t(__ldg(scales + idx)) : 0u) | (v1 ? uint32_t(__ldg(scales + idx + 1)) << 16 : 0u);
-          b_w[hw] = (v0 ? uint32_t(__ldg(biases + idx)) : 0u) | (v1 ? uint32_t(__ldg(biases + idx + 1)) << 16 : 0u);
+          const bool v0 = ga < G, v1 = ga + 1 < G;
+          s_w[hw] = (v0 ? uint32_t(__ldg(a.scales + idx)) : 0u) |
+                    (v1 ? uint32_t(__ldg(a.scales + idx + 1)) << 16 : 0u);
+          b_w[hw] = (v0 ? uint32_t(__ldg(a.biases + idx)) : 0u) |
+                    (v1 ? uint32_t(__ldg(a.biases + idx + 1)) << 16 : 0u);
         }
       } else {
         const int off = r * 16 + (gs & 7) * 2;  // (gs & 7) is 0 or 4: 8-byte aligned
-        const uint2 sv = *reinterpret_cast<const uint2 *>(st + C::C_BYTES + off);
-        const uint2 bv = *reinterpret_cast<const uint2 *>(st + C::C_BYTES + C::SB_BYTES + off);
+        const uint2 sv = *reinterpret_cast<const uint2 *>(cb + C::C_BYTES + off);
+        const uint2 bv = *reinterpret_cast<const uint2 *>(cb + C::C_BYTES + C::SB_BYTES + off);
         s_w[0] = sv.x; s_w[1] = sv.y; b_w[0] = bv.x; b_w[1] = bv.y;
       }
       // the stage's 32 packed words of this row, then release the codes slot
       uint32_t words[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int chunk = c ^ (r & 7);  // TMA 128-byte swizzle
-        const uint4 v = *reinterpret_cast<const uint4 *>(st + r * 128 + chunk * 16);
-        words[4 * c + 0] = v.x; words[4 * c + 1] = v.y; words[4 * c + 2] = v.z; words[4 * c + 3] = v.w;
+      for (int cc = 0; cc < 8; ++cc) {
+        const int chunk = cc ^ (r & 7);  // TMA 128-byte swizzle
+        const uint4 v = *reinterpret_cast<const uint4 *>(cb + r * 128 + chunk * 16);
+        words[4 * cc + 0] = v.x; words[4 * cc + 1] = v.y; words[4 * cc + 2] = v.z; words[4 * cc + 3] = v.w;
       }
+      // the slot is refilled by TMA (async proxy): order these generic-proxy reads
+      // before that write, which the mbarrier release alone does not do
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&free_c[cs]);
       // the A slot is free once the MMAs of this warpgroup's previous stage completed
@@ -310,50 +371,117 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         for (int wj = 0; wj < 8; ++wj) {
           uint32_t o[4];
           dequant_word(words[gl * 8 + wj], s2, b2, o);
-          a[4 * wj + 0] = o[0]; a[4 * wj + 1] = o[1]; a[4 * wj + 2] = o[2]; a[4 * wj + 3] = o[3];
+          wt[4 * wj + 0] = o[0]; wt[4 * wj + 1] = o[1]; wt[4 * wj + 2] = o[2]; wt[4 * wj + 3] = o[3];
         }
-        tmem_st32(lane_base + C::A_COL0 + (wg * C::SG + gl) * C::GA, a);
+        tmem_st32(lane_base + C::A_COL0 + (wg * C::SG + gl) * C::GA, wt);
       }
-      // tcgen05.st reads its source registers at issue (a is reused above); the
+      // tcgen05.st reads its source registers at issue (wt is reused above); the
       // stores must only have reached TMEM before the issuers are told
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[wg]);
-      if (!ok) break;
       ++ai;
       cs += C::WGS;
       if (cs >= C::NC) { cs -= C::NC; cphase ^= 1u; }
     }
-    // ---------------- epilogue part 1: accumulator -> y or partials
-    if (wg == 0 && ok && nst > 0 && warp_wait(acc_full, 0)) {
-      tc_fence_after();
-      float *red = reinterpret_cast<float *>(smem);  // [NP][128], the stage area is free now
-      // accumulator u holds data once some stage has a group in its part
+  } else if (warp < 4) {
+    // ---------------- epilogue: one pass per segment of the CTA's range, 16
+    // accumulator columns (tokens) at a time
+    const int q = warp;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    int li = 0, seg = 0;
+    int tile, st0;
+    unit(0, tile, st0);
+    while (li < L) {
+      const int seg_len = min(L - li, a.nst - st0);
+      const bool whole = st0 == 0 && seg_len == a.nst;
+      // issuer u accumulated iff some stage of the segment has a group in its share
+      const int max_ng = min(C::SG, G - st0 * C::SG);
       int nacc = 1;
-      while (nacc < C::NI && g1 - g0 > nacc * C::GPI) ++nacc;
-#pragma unroll
-      for (int c0 = 0; c0 < NP; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(lane_base + c0, v);
-        tmem_wait_ld();
-        for (int u = 1; u < nacc; ++u) {
-          uint32_t v1[16];
-          tmem_ld16(lane_base + u * NP + c0, v1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) + __uint_as_float(v1[e]));
-        }
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int t = c0 + e;
-          if (splits == 1) {
-            if (t < M) y[(size_t)t * ldy + row] = float_to_bf16_bits(__uint_as_float(v[e]));
-          } else {
-            red[t * 128 + r] = __uint_as_float(v[e]);
+      while (nacc < C::NI && max_ng > nacc * C::GPI) ++nacc;
+      int clo = c, parts = 1;
+      if (!whole) {
+        clo = part.c_lo(tile);
+        parts = part.c_hi(tile) - clo + 1;
+      }
+      const int p = c - clo;  // this CTA's part of the tile
+      float *pbase = a.partials + ((size_t)tile * a.maxp) * (NP * 128);
+      uint32_t *fbase = a.flags + (size_t)tile * a.maxp;
+      if (!warp_wait(acc_full, (uint32_t)(seg & 1))) break;
+      tc_fence_after();
+      if (!whole && p == 0) {
+        // the first part ends this CTA's range: wait for the later parts
+        if (threadIdx.x == 0) {
+          for (int pp = 1; pp < parts; ++pp) {
+            const unsigned long long t0 = globaltimer_ns();
+            while (ld_acquire_gpu(fbase + pp) == 0u) {
+              if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
+            }
           }
         }
+        named_barrier_sync(1, 128);
+        __threadfence();
       }
+      const int row = tile * C::ROWS + r;
+      // CW accumulator columns (tokens) at a time, every accumulator's chunk in
+      // flight at once behind one wait (8 columns with 4 accumulators keeps it
+      // to 32 registers)
+      constexpr int CW = C::NI > 2 ? 8 : 16;
+#pragma unroll 1
+      for (int c0 = 0; c0 < NP; c0 += CW) {
+        uint32_t tv[C::NI][CW];
+#pragma unroll
+        for (int uu = 0; uu < C::NI; ++uu)
+          if (uu < nacc) {
+            if constexpr (CW == 8) tmem_ld8(lane_base + uu * NP + c0, tv[uu]);
+            else tmem_ld16(lane_base + uu * NP + c0, tv[uu]);
+          }
+        tmem_wait_ld();
+        float v[CW];
+#pragma unroll
+        for (int e = 0; e < CW; ++e) v[e] = __uint_as_float(tv[0][e]);
+#pragma unroll
+        for (int uu = 1; uu < C::NI; ++uu)
+          if (uu < nacc) {
+#pragma unroll
+            for (int e = 0; e < CW; ++e) v[e] += __uint_as_float(tv[uu][e]);
+          }
+        if (!whole && p > 0) {
+          float *dst = pbase + (size_t)p * (NP * 128) + (size_t)c0 * 128 + r;
+#pragma unroll
+          for (int e = 0; e < CW; ++e) dst[e * 128] = v[e];
+          continue;
+        }
+        if (!whole) {
+          for (int pp = 1; pp < parts; ++pp) {
+            const float *src = pbase + (size_t)pp * (NP * 128) + (size_t)c0 * 128 + r;
+#pragma unroll
+            for (int e = 0; e < CW; ++e) v[e] += __ldcg(src + e * 128);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < CW; ++e)
+          if (c0 + e < a.M) a.y[(size_t)(c0 + e) * a.ldy + row] = float_to_bf16_bits(v[e]);
+      }
+      // the accumulators are read: the issuers may start the next segment
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      if (!whole && p > 0) {
+        // publish this part: its partial above, then its flag
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 0) st_release_gpu(fbase + p, 1u);
+      } else if (!whole) {
+        // leave the flags clear for the next call
+        named_barrier_sync(1, 128);
+        for (int pp = 1 + (int)threadIdx.x; pp < parts; pp += 128) fbase[pp] = 0u;
+      }
+      li += seg_len;
+      ++seg;
+      step(tile, st0, seg_len);
     }
   }
   tc_fence_before();
@@ -363,30 +491,47 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
-  if (splits > 1) {
-    // ---------------- epilogue part 2: reduce the cluster's partials (DSMEM)
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    float *red = reinterpret_cast<float *>(smem);
-    const int rank = (int)cluster.block_rank();
-    const int total = NP * 128;
-    const int per = (total + splits - 1) / splits;
-    const int e0 = rank * per, e1 = min(total, e0 + per);
-    for (int e = e0 + (int)threadIdx.x; e < e1; e += C::THREADS) {
-      const int t = e >> 7;
-      if (t >= M) continue;
-      float acc = 0.f;
-      for (int rr = 0; rr < splits; ++rr) acc += cluster.map_shared_rank(red, rr)[e];
-      y[(size_t)t * ldy + n0 + (e & 127)] = float_to_bf16_bits(acc);
-    }
-    cluster.sync();
-  }
+}
+
+// The workspace starts with a fixed flag region for every shape: partials of
+// one call must never land where another shape's call keeps its flags (the
+// region is only ever written with flag stores, so it stays zero between
+// calls), and the partials follow it.
+constexpr size_t kFlagRegionBytes = 64 * 1024;
+
+// Grid and workspace of one call.
+struct TsPlan {
+  long long U;
+  int P, nst, tiles, maxp;
+  size_t flag_bytes, part_bytes;
+};
+
+template <int NP>
+TsPlan plan_ts(int M, int N, int K) {
+  (void)M;
+  TsPlan p;
+  p.tiles = N / 128;
+  p.nst = (K / 64 + 3) / 4;
+  p.U = (long long)p.tiles * p.nst;
+  long long P = sm_count();
+  if (P > p.U / 2) P = p.U / 2;  // at least two stages per CTA
+  if (P < 1) P = 1;
+  p.P = (int)P;
+  const long long per = p.U / p.P;  // the shortest range
+  p.maxp = (int)((p.nst + per - 1) / per) + 1;
+  p.flag_bytes = kFlagRegionBytes;  // tiles * maxp flags must fit: checked at launch
+  p.part_bytes = (size_t)p.tiles * p.maxp * NP * 128 * sizeof(float);
+  return p;
 }
 
 template <int NP>
 int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-              int K, int ldy, cudaStream_t st) {
+              int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st) {
   using C = TsCfg<NP>;
+  const TsPlan plan = plan_ts<NP>(M, N, K);
+  if ((size_t)plan.tiles * plan.maxp * sizeof(uint32_t) > kFlagRegionBytes) return TSB_EUNSUPPORTED;
+  if (!ws || ws_bytes < plan.flag_bytes + plan.part_bytes) return TSB_EWORKSPACE;
+  if (!aligned(ws, 256)) return TSB_EINVAL;
   CUtensorMap tx, tw;
   if (make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64, NP,
                    CU_TENSOR_MAP_SWIZZLE_128B) != TSB_OK)
@@ -415,37 +560,53 @@ int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uin
       return TSB_ECUDA;
     attr_dev = dev;
   }
-  const int tiles = N / 128;
-  const int nst_all = (int)((G64 + C::SG - 1) / C::SG);
-  // one CTA per SM (all of TMEM): split K so that the grid fills the SMs in one wave
-  int splits = tiles >= sm_count() ? 1 : sm_count() / tiles;
-  if (splits > 8) splits = 8;
-  while (splits > 1 && nst_all / splits < 2) --splits;
+  TsArgs a;
+  a.scales = s;
+  a.biases = b;
+  a.y = y;
+  a.flags = static_cast<uint32_t *>(ws);
+  a.partials = reinterpret_cast<float *>(static_cast<unsigned char *>(ws) + plan.flag_bytes);
+  a.U = plan.U;
+  a.M = M; a.N = N; a.K = K; a.ldy = ldy;
+  a.P = plan.P;
+  a.nst = plan.nst;
+  a.maxp = plan.maxp;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles, splits, 1);
+  cfg.gridDim = dim3(plan.P, 1, 1);
   cfg.blockDim = dim3(C::THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
+  // the first part of a split tile waits for the later parts: all CTAs must be
+  // co-resident (P <= #SM, one CTA per SM), which a cooperative launch guarantees
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = splits;
-  attr[0].val.clusterDim.z = 1;
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_ts_kernel<NP>, tx, tw, tsc, tbi, s, b, y, M, N, K, ldy, splits);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_ts_kernel<NP>, tx, tw, tsc, tbi, a);
   return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 }  // namespace
 
+// Workspace of the verify path: completion flags (zero between calls) and the
+// float partials of split tiles.
+size_t qmm_ts_workspace_bytes(int M, int N, int K) {
+  TsPlan p;
+  if (M <= 16) p = plan_ts<16>(M, N, K);
+  else if (M <= 32) p = plan_ts<32>(M, N, K);
+  else if (M <= 64) p = plan_ts<64>(M, N, K);
+  else p = plan_ts<128>(M, N, K);
+  return p.flag_bytes + p.part_bytes;
+}
+
 // M in [1, 128]: tokens padded to a multiple of 16 for the MMA's N.
 int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-           int K, int ldy, cudaStream_t st) {
-  if (M <= 16) return launch_ts<16>(x, w, s, b, y, M, N, K, ldy, st);
-  if (M <= 32) return launch_ts<32>(x, w, s, b, y, M, N, K, ldy, st);
-  if (M <= 64) return launch_ts<64>(x, w, s, b, y, M, N, K, ldy, st);
-  return launch_ts<128>(x, w, s, b, y, M, N, K, ldy, st);
+           int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st) {
+  if (M <= 16) return launch_ts<16>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
+  if (M <= 32) return launch_ts<32>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
+  if (M <= 64) return launch_ts<64>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
+  return launch_ts<128>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
 }
 
 unsigned int status_ts(bool reset) {

@@ -42,6 +42,24 @@ def workspace(nbytes: int, device) -> torch.Tensor:
     return buf
 
 
+_QWS: dict[int, torch.Tensor] = {}
+
+
+def qmm_workspace(nbytes: int, device) -> torch.Tensor:
+    """The per-device workspace of the verify qmm: zero-initialised, used for nothing else.
+
+    It holds completion flags the kernel leaves zero after every call, so it is
+    allocated with zeros once (and again, zeroed, when it has to grow) and never
+    shared with the attention scratch."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    buf = _QWS.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _QWS[idx] = buf
+    return buf
+
+
 def _stream(t: torch.Tensor) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
@@ -79,8 +97,7 @@ def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: i
     if out is None:
         out = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=x.device)
     lib = _lib.load()
-    ws_n = lib.tsb_qmm_workspace_bytes(m, n, k)
-    ws = workspace(ws_n, x.device)
+    ws = qmm_workspace(lib.tsb_qmm_workspace_bytes(m, n, k), x.device)
     st = lib.tsb_qmm_w4g64(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), m, n, k, n,
                            _ptr(ws), ws.numel(), _stream(x))
     if check(st, "tsb_qmm_w4g64") == TSB_EUNSUPPORTED:
@@ -95,7 +112,7 @@ def quantized_matmul_into(x2, w, scales, biases, y, ldy: int):
     m, k = x2.shape
     n = w.shape[0]
     lib = _lib.load()
-    ws = workspace(lib.tsb_qmm_workspace_bytes(m, n, k), x2.device)
+    ws = qmm_workspace(lib.tsb_qmm_workspace_bytes(m, n, k), x2.device)
     st = lib.tsb_qmm_w4g64(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(y), m, n, k, ldy,
                            _ptr(ws), ws.numel(), _stream(x2))
     return check(st, "tsb_qmm_w4g64")

@@ -73,5 +73,7 @@ def test_workspace_sizes_are_host_computable(lib_built):
     from tsb import _lib
 
     lib = _lib.load()
-    assert lib.tsb_qmm_workspace_bytes(16, 6144, 5120) == 0  # the qmm paths need no scratch
+    # verify path: completion flags + partials of the row tiles split across CTAs
+    assert lib.tsb_qmm_workspace_bytes(16, 6144, 5120) > 0
+    assert lib.tsb_qmm_workspace_bytes(4096, 6144, 5120) == 0  # the prefill GEMM needs none
     assert lib.tsb_tree_attn_workspace_bytes(1, 32, 24, 4, 256, 32800, 0) > 0

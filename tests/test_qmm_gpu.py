@@ -156,6 +156,53 @@ def test_qmm_prefill_config3_sampled(nk):
     assert_close_rel(got, ref, REL_TIGHT, f"prefill {nk}")
 
 
+@pytest.mark.parametrize("m,n,k", [(16, 6144, 5120), (1, 1024, 5120), (64, 384, 17408), (128, 128, 640)])
+def test_qmm_split_tiles_and_workspace_left_clear(m, n, k):
+    """Shapes whose row tiles are split across CTAs (stream-K parts joined through
+    the workspace): full oracle check, twice in a row, and the workspace's
+    completion flags are all zero again afterwards."""
+    import tsb
+    from tsb import _lib, ops
+
+    rng = np.random.default_rng(9100 + m + n + k)
+    x = gen.x_bf16(rng, m, k)
+    wq, s, b = gen.weights_w4g64(rng, n, k)
+    ref = qmm.qmm(x, wq, s, b)
+    for _ in range(2):
+        y = _run(x, wq, s, b)
+        assert_close_rel(y, ref, REL_TIGHT, f"split {m}x{n}x{k}")
+    lib = _lib.load()
+    nbytes = lib.tsb_qmm_workspace_bytes(m, n, k)
+    ws = ops.qmm_workspace(nbytes, "cuda")
+    torch.cuda.synchronize()
+    # flags are [tiles][maxp] uint32 words at the start of a fixed 64 KB flag
+    # region (the kernel's plan for this device); partials follow it
+    tiles, nst = n // 128, (k // 64 + 3) // 4
+    units = tiles * nst
+    ctas = max(1, min(torch.cuda.get_device_properties(0).multi_processor_count, units // 2))
+    maxp = -(-nst // (units // ctas)) + 1
+    flags = ws[: 64 * 1024].view(torch.int32).cpu().numpy()
+    assert tiles * maxp <= flags.size
+    assert not np.any(flags), "completion flags left set"
+
+
+def test_qmm_workspace_too_small_refused():
+    from tsb import _lib
+
+    lib = _lib.load()
+    x = torch.zeros(16, 5120, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(6144, 640, dtype=torch.int32, device="cuda")
+    s = torch.zeros(6144, 80, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(16, 6144, dtype=torch.bfloat16, device="cuda")
+    small = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    st = lib.tsb_qmm_w4g64(x.data_ptr(), w.data_ptr(), s.data_ptr(), s.data_ptr(), y.data_ptr(), 16, 6144, 5120,
+                           6144, small.data_ptr(), small.numel(), None)
+    assert st == _lib.TSB_EWORKSPACE
+    st = lib.tsb_qmm_w4g64(x.data_ptr(), w.data_ptr(), s.data_ptr(), s.data_ptr(), y.data_ptr(), 16, 6144, 5120,
+                           6144, None, 0, None)
+    assert st == _lib.TSB_EWORKSPACE
+
+
 def test_device_status_clean_after_runs():
     """No bounded device-side wait has given up during the tests."""
     from tsb import _lib
