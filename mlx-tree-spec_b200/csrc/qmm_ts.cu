@@ -134,6 +134,13 @@ TSB_HD uint32_t ld_acquire_gpu(const uint32_t *p) {
 TSB_HD void st_release_gpu(uint32_t *p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// 16-byte global -> shared copy through L2 (cp.async.cg), completed by cp_async_wait_all.
+TSB_HD void cp_async_cg16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+TSB_HD void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
 
 template <int NP>
 __global__ void __launch_bounds__(TsCfg<NP>::THREADS, 1)
@@ -411,18 +418,30 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       uint32_t *fbase = a.flags + (size_t)tile * a.maxp;
       if (!warp_wait(acc_full, (uint32_t)(seg & 1))) break;
       tc_fence_after();
+      // first part: wait for the later parts (one thread per flag, in parallel),
+      // then pull all their partials into the stage area (idle once the last
+      // segment is accumulated) with one round of cp.async
+      bool staged = false;
+      const float *sp = reinterpret_cast<const float *>(smem);
       if (!whole && p == 0) {
-        // the first part ends this CTA's range: wait for the later parts
-        if (threadIdx.x == 0) {
-          for (int pp = 1; pp < parts; ++pp) {
-            const unsigned long long t0 = globaltimer_ns();
-            while (ld_acquire_gpu(fbase + pp) == 0u) {
-              if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
-            }
+        if ((int)threadIdx.x < parts - 1) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (ld_acquire_gpu(fbase + 1 + threadIdx.x) == 0u) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
           }
         }
         named_barrier_sync(1, 128);
         __threadfence();
+        const size_t bytes = (size_t)(parts - 1) * NP * 512;
+        if (bytes <= (size_t)C::STAGE_AREA) {
+          staged = true;
+          const unsigned char *src = reinterpret_cast<const unsigned char *>(pbase + (size_t)NP * 128);
+          const uint32_t dst = smem_addr(smem);
+          for (size_t off = (size_t)threadIdx.x * 16; off < bytes; off += 128 * 16)
+            cp_async_cg16(dst + (uint32_t)off, src + off);
+          cp_async_wait_all();
+          named_barrier_sync(1, 128);
+        }
       }
       const int row = tile * C::ROWS + r;
       // CW accumulator columns (tokens) at a time, every accumulator's chunk in
@@ -454,11 +473,30 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
           for (int e = 0; e < CW; ++e) dst[e * 128] = v[e];
           continue;
         }
-        if (!whole) {
+        if (staged) {
           for (int pp = 1; pp < parts; ++pp) {
-            const float *src = pbase + (size_t)pp * (NP * 128) + (size_t)c0 * 128 + r;
+            const float *src = sp + (size_t)(pp - 1) * (NP * 128) + (size_t)c0 * 128 + r;
 #pragma unroll
-            for (int e = 0; e < CW; ++e) v[e] += __ldcg(src + e * 128);
+            for (int e = 0; e < CW; ++e) v[e] += src[e * 128];
+          }
+        } else if (!whole) {
+          // two parts' chunks in flight per round (L2 hits, one latency each)
+          constexpr int PU = 2;
+          for (int pp0 = 1; pp0 < parts; pp0 += PU) {
+            float t[PU][CW];
+#pragma unroll
+            for (int q2 = 0; q2 < PU; ++q2)
+              if (pp0 + q2 < parts) {
+                const float *src = pbase + (size_t)(pp0 + q2) * (NP * 128) + (size_t)c0 * 128 + r;
+#pragma unroll
+                for (int e = 0; e < CW; ++e) t[q2][e] = __ldcg(src + e * 128);
+              }
+#pragma unroll
+            for (int q2 = 0; q2 < PU; ++q2)
+              if (pp0 + q2 < parts) {
+#pragma unroll
+                for (int e = 0; e < CW; ++e) v[e] += t[q2][e];
+              }
           }
         }
 #pragma unroll
