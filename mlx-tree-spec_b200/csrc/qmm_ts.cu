@@ -81,7 +81,11 @@ struct TsCfg {
   static constexpr int NC = (NC_FIT > 12 ? 12 : NC_FIT) / WGS * WGS;  // codes slots, a multiple of WGS
   static constexpr int X_AREA = NC * CSLOT_BYTES;
   static constexpr int STAGE_AREA = X_AREA + NX * XSLOT_BYTES;
-  static constexpr int A_COL0 = (NI * NP + 31) / 32 * 32;  // accumulators in [0, NI NP), A slots after
+  static constexpr int ACC_COLS = (NI * NP + 31) / 32 * 32;  // one set of NI accumulators
+  // two accumulator sets when TMEM has room: segment k+1 accumulates while the
+  // epilogue reads segment k
+  static constexpr int NB = 2 * ACC_COLS + WGS * SG * 32 <= 512 ? 2 : 1;
+  static constexpr int A_COL0 = NB * ACC_COLS;      // accumulators in [0, NB ACC_COLS), A slots after
   static constexpr int GA = 32;                    // per group: 64 bf16 weights per row
   static constexpr int TMEM_COLS = 512;
   static constexpr int CODES_WARP = 4, X_WARP = 5, DQ_WARP0 = 8;  // epilogue: warps 0-3
@@ -157,9 +161,9 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   uint64_t *free_x = full_x + C::NX;             // [NX] MMAs that read the slot are done
   uint64_t *a_full = free_x + C::NX;             // [WGS] stage written into TMEM
   uint64_t *a_empty = a_full + C::WGS;           // [WGS] MMAs done with the stage slot
-  uint64_t *acc_full = a_empty + C::WGS;         // segment accumulated
-  uint64_t *acc_empty = acc_full + 1;            // accumulators read by the epilogue
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
+  uint64_t *acc_full = a_empty + C::WGS;         // [NB] segment accumulated in set b
+  uint64_t *acc_empty = acc_full + C::NB;        // [NB] set b read by the epilogue
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + C::NB);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const Part part{a.U, a.P, a.nst};
@@ -195,8 +199,10 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       mbar_init(&a_full[b], 4);      // the 4 warps of the owning warpgroup
       mbar_init(&a_empty[b], C::NI);  // every MMA issuer
     }
-    mbar_init(acc_full, C::NI);
-    mbar_init(acc_empty, 4);  // the epilogue warps
+    for (int b = 0; b < C::NB; ++b) {
+      mbar_init(&acc_full[b], C::NI);
+      mbar_init(&acc_empty[b], 4);  // the epilogue warps
+    }
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -269,17 +275,21 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     const int u = warp < 20 ? warp - 6 : warp - 18;
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, NP);
-      const uint32_t dacc = tmem_base + (uint32_t)(u * NP);
       bool ok = true, first = true;
       int seg = 0;
+      uint32_t dacc = tmem_base + (uint32_t)(u * NP);  // accumulator u of set seg % NB
       Ring ring, aring;
       int tile, st;
       unit(0, tile, st);
       for (int li = 0; li < L && ok; ++li, ring.next(C::NX), aring.next(C::WGS), step(tile, st, 1)) {
         if (li > 0 && st == 0) {
-          // a new segment: the epilogue must have read the accumulators
-          ok = mbar_wait(acc_empty, (uint32_t)((seg - 1) & 1));
-          if (!ok) break;
+          // a new segment in set seg % NB: the epilogue must have read that set's
+          // previous segment (seg - NB)
+          if (seg >= C::NB) {
+            ok = mbar_wait(&acc_empty[seg % C::NB], (uint32_t)(((seg / C::NB) - 1) & 1));
+            if (!ok) break;
+          }
+          dacc = tmem_base + (uint32_t)((seg % C::NB) * C::ACC_COLS + u * NP);
           first = true;
         }
         ok = mbar_wait(&full_x[ring.slot], ring.phase) && mbar_wait(&a_full[aring.slot], aring.phase);
@@ -301,7 +311,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         mma_commit(&a_empty[aring.slot]);
         mma_commit(&free_x[ring.slot]);
         if (li == L - 1 || st == a.nst - 1) {  // the segment's last stage
-          mma_commit(acc_full);
+          mma_commit(&acc_full[seg % C::NB]);
           ++seg;
         }
       }
@@ -416,8 +426,9 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       const int p = c - clo;  // this CTA's part of the tile
       float *pbase = a.partials + ((size_t)tile * a.maxp) * (NP * 128);
       uint32_t *fbase = a.flags + (size_t)tile * a.maxp;
-      if (!warp_wait(acc_full, (uint32_t)(seg & 1))) break;
+      if (!warp_wait(&acc_full[seg % C::NB], (uint32_t)((seg / C::NB) & 1))) break;
       tc_fence_after();
+      const uint32_t acc_base = lane_base + (uint32_t)((seg % C::NB) * C::ACC_COLS);
       // first part: wait for the later parts (one thread per flag, in parallel),
       // then pull all their partials into the stage area (idle once the last
       // segment is accumulated) with one round of cp.async
@@ -454,8 +465,8 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
 #pragma unroll
         for (int uu = 0; uu < C::NI; ++uu)
           if (uu < nacc) {
-            if constexpr (CW == 8) tmem_ld8(lane_base + uu * NP + c0, tv[uu]);
-            else tmem_ld16(lane_base + uu * NP + c0, tv[uu]);
+            if constexpr (CW == 8) tmem_ld8(acc_base + uu * NP + c0, tv[uu]);
+            else tmem_ld16(acc_base + uu * NP + c0, tv[uu]);
           }
         tmem_wait_ld();
         float v[CW];
@@ -506,7 +517,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       // the accumulators are read: the issuers may start the next segment
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty);
+      if (lane == 0) mbar_arrive(&acc_empty[seg % C::NB]);
       if (!whole && p > 0) {
         // publish this part: its partial above, then its flag
         __threadfence();
