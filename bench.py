@@ -129,7 +129,7 @@ def dist_setup():
         torch.cuda.set_device(local)
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     return world, rank, local
@@ -284,6 +284,10 @@ def run_tsb(args):
     barrier(world)
     ms = t0.elapsed_time(t1) / args.steps
     clk = clocks.stop()
+    # a CUDA graph that holds NCCL calls must be released before the process
+    # group is destroyed, or the exit waits for good
+    del g
+    torch.cuda.synchronize()
     ms = max_over_ranks(ms, world)
     value = total_bytes / (ms * 1e-3) / 1e12
 
@@ -395,6 +399,8 @@ def run_tsb(args):
     if world > 1:
         import torch.distributed as dist
 
+        torch.cuda.synchronize()
+        dist.barrier()
         dist.destroy_process_group()
 
 
