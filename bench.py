@@ -180,8 +180,26 @@ def copies_needed(ns, k, l2_bytes=126 * 2**20, factor=2.5):
 
 # ------------------------------------------------------------------ tsb arm
 
+def make_cache(fmt, kf, vf, n_kv):
+    """A config-4 KV cache of the given format from float K/V (B, Hkv, rows, D)."""
+    import torch
+
+    import tsb
+
+    if fmt == "bf16":
+        return tsb.KVCache(kf.to(torch.bfloat16), vf.to(torch.bfloat16), n_kv)
+    if fmt == "ref_q8":
+        kq, ks = tsb.quantize_rows(kf)
+        vq, vs = tsb.quantize_rows(vf)
+        return tsb.Q8KVCache(kq, vq, ks, vs, n_kv)
+    kw, ks, kb = tsb.quantize_g64(kf)
+    vw, vs, vb = tsb.quantize_g64(vf)
+    return tsb.MLXQ8KVCache(kw, vw, ks, kb, vs, vb, n_kv)
+
+
 def run_profile_attn(args):
-    """Config-4 tree attention (B=1, L=32768, T=32, 24q/4kv, D=256, bf16 KV): --warmup calls, then one."""
+    """Config-4 tree attention (B=1, L=32768, T=32, 24q/4kv, D=256, KV format
+    --attn-kv): --warmup calls, then one."""
     import numpy as np
     import torch
 
@@ -193,15 +211,16 @@ def run_profile_attn(args):
     bsz, L, t, hq, hkv, d = 1, 32768, 32, 24, 4, 256
     n_kv = L + t
     g = torch.Generator(device="cuda").manual_seed(3)
-    k = torch.randn(bsz, hkv, n_kv, d, device="cuda", generator=g).to(torch.bfloat16)
-    v = torch.randn(bsz, hkv, n_kv, d, device="cuda", generator=g).to(torch.bfloat16)
+    kf = torch.randn(bsz, hkv, n_kv, d, device="cuda", generator=g)
+    vf = torch.randn(bsz, hkv, n_kv, d, device="cuda", generator=g)
     q = torch.randn(bsz, hq, t, d, device="cuda", generator=g).to(torch.bfloat16)
     parents = torch.from_numpy(np.stack([gen.tree_parents(np.random.default_rng(i), t) for i in range(bsz)])).cuda()
-    cache = tsb.KVCache(k, v, n_kv)
+    cache = make_cache(args.attn_kv, kf, vf, n_kv)
+    del kf, vf
     for _ in range(args.warmup + 1):
         tsb.tree_flash(q, cache, d**-0.5, parents=parents)
     torch.cuda.synchronize()
-    print(json.dumps({"profile": "attn", "calls": args.warmup + 1}))
+    print(json.dumps({"profile": "attn", "kv": args.attn_kv, "calls": args.warmup + 1}))
 
 
 def run_tsb(args):
@@ -475,19 +494,15 @@ def run_secondary(pool, xs, hbm_peak, bf16_peak):
     from oracle import gen
     import numpy as np
 
-    for (bsz, L, fmt) in ((1, 32768, "bf16"), (4, 8192, "bf16"), (1, 32768, "mlx_q8"), (4, 8192, "mlx_q8")):
+    for (bsz, L, fmt) in ((1, 32768, "bf16"), (4, 8192, "bf16"), (1, 32768, "mlx_q8"), (4, 8192, "mlx_q8"),
+                          (1, 32768, "ref_q8")):
         t, hq, hkv, d = 32, 24, 4, 256
         n_kv = L + t
         caches = []
         for i in range(4):  # rotate 4 caches so K/V are not L2-resident
             kf = torch.randn(bsz, hkv, n_kv, d, device="cuda")
             vf = torch.randn(bsz, hkv, n_kv, d, device="cuda")
-            if fmt == "bf16":
-                caches.append(tsb.KVCache(kf.to(torch.bfloat16), vf.to(torch.bfloat16), n_kv))
-            else:
-                kw, ks, kb = tsb.quantize_g64(kf)
-                vw, vs, vb = tsb.quantize_g64(vf)
-                caches.append(tsb.MLXQ8KVCache(kw, vw, ks, kb, vs, vb, n_kv))
+            caches.append(make_cache(fmt, kf, vf, n_kv))
             del kf, vf
         q = torch.randn(bsz, hq, t, d, device="cuda").to(torch.bfloat16)
         parents = torch.from_numpy(np.stack([gen.tree_parents(np.random.default_rng(i), t) for i in range(bsz)])).cuda()
@@ -497,7 +512,7 @@ def run_secondary(pool, xs, hbm_peak, bf16_peak):
                 tsb.tree_flash(q, c, d**-0.5, parents=parents)
 
         us = time_graph(f) / len(caches)
-        row = 512 if fmt == "bf16" else 272
+        row = {"bf16": 512, "mlx_q8": 272, "ref_q8": 260}[fmt]
         byts = bsz * n_kv * hkv * row * 2 + 2 * bsz * t * hq * d * 2
         fl = 4.0 * bsz * t * hq * n_kv * d
         out[f"attn_B{bsz}_L{L}_{fmt}"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1),
@@ -601,7 +616,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--profile", choices=["qmm", "attn"], default=None,
                     help="profiling driver for ncu: --warmup eager steps, then exactly one eager step "
-                         "(qmm: the 15 sweep calls; attn: one config-4 B=1 L=32768 bf16 call); no timing")
+                         "(qmm: the 15 sweep calls; attn: one config-4 B=1 L=32768 call); no timing")
+    ap.add_argument("--attn-kv", choices=["bf16", "mlx_q8", "ref_q8"], default="bf16",
+                    help="KV format of --profile attn")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,5 +1,8 @@
 // Tree-mask flash attention: T tree-node queries of G = Hq/Hkv heads over one
-// KV head's long prefix plus the nodes' own rows.
+// KV head's long prefix plus the nodes' own rows. Calls go to the tcgen05
+// kernel (attn_tc.cu) whenever it takes them; the warp-MMA kernel below serves
+// the rest (MLX 8-bit caches with an odd capacity or unaligned scale/bias
+// rows) and owns the entry points, the plan and the split combine.
 //
 // Semantics follow mlx-tree-spec `tree_flash` (src/mlx_tree_spec/tree_flash.py:
 // 151-196; visibility at 40-45): key row j < n_kv is visible to node t iff it
@@ -24,6 +27,7 @@
 // MLX_Q8_G64 rows are dequantized (s * q + b, rounded to bf16) into the tile.
 #include "common.cuh"
 
+#include <algorithm>
 #include <mutex>
 
 namespace tsb {
@@ -499,23 +503,25 @@ size_t attn_smem_bytes() {
 }  // namespace
 
 void plan_attn_tc(int B, int T, int Hq, int Hkv, int n_kv, int &row_blocks, int &splits, int &tiles_per_split);
-int launch_attn_tc(const uint16_t *q, const uint16_t *k, const uint16_t *v, const int32_t *parents,
-                   const unsigned long long *bits, int B, int T, int Hq, int Hkv, int n_kv, int tail, int cap,
-                   float scale, uint16_t *out, float *lse, float *part_o, float *part_ml, cudaStream_t st);
+bool attn_tc_supported(int kv_format, int cap, const void *ks, const void *kb, const void *vs, const void *vb);
+int launch_attn_tc(int kv_format, const uint16_t *q, const void *k, const void *ks, const void *kb, const void *v,
+                   const void *vs, const void *vb, const int32_t *parents, const unsigned long long *bits, int B,
+                   int T, int Hq, int Hkv, int n_kv, int tail, int cap, float scale, uint16_t *out, float *lse,
+                   float *part_o, float *part_ml, cudaStream_t st);
 
 }  // namespace tsb
 
 using namespace tsb;
 
-// Key splits of a call: the tcgen05 kernel for bf16 KV, the warp-MMA kernel
-// (8-bit formats, dequantized while staged) otherwise.
+// Key splits of a call. bf16 and reference-int8 KV always run the tcgen05
+// kernel; MLX 8-bit KV runs it when its scale/bias rows can be bulk-copied
+// (attn_tc_supported) and the warp-MMA kernel otherwise, so its workspace
+// covers whichever of the two plans splits more.
 static int attn_splits(int B, int T, int Hq, int Hkv, int n_kv, int kv_format) {
-  if (kv_format == TSB_KV_BF16) {
-    int rb, splits, tps;
-    plan_attn_tc(B, T, Hq, Hkv, n_kv, rb, splits, tps);
-    return splits;
-  }
-  return plan_attn(B, T, Hq, Hkv, n_kv).splits;
+  int rb, splits, tps;
+  plan_attn_tc(B, T, Hq, Hkv, n_kv, rb, splits, tps);
+  if (kv_format == TSB_KV_MLX_Q8_G64) splits = std::max(splits, plan_attn(B, T, Hq, Hkv, n_kv).splits);
+  return splits;
 }
 
 extern "C" size_t tsb_tree_attn_workspace_bytes(int B, int T, int Hq, int Hkv, int D, int n_kv, int kv_format) {
@@ -547,9 +553,10 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
 
   const size_t rows = (size_t)B * Hq * T;
   cudaStream_t st = (cudaStream_t)stream;
-  if (kv_format == TSB_KV_BF16) {
+  if (attn_tc_supported(kv_format, kv_capacity, k_scales, k_biases, v_scales, v_biases)) {
     if (!(scale > 0.f)) return TSB_EUNSUPPORTED;  // the kernel takes row maxima of unscaled scores
-    const int splits = attn_splits(B, T, Hq, Hkv, n_kv, kv_format);
+    int rb, splits, tps;
+    plan_attn_tc(B, T, Hq, Hkv, n_kv, rb, splits, tps);
     float *part_o = nullptr, *part_ml = nullptr;
     if (splits > 1) {
       const size_t need = tsb_tree_attn_workspace_bytes(B, T, Hq, Hkv, D, n_kv, kv_format);
@@ -558,7 +565,7 @@ extern "C" int tsb_tree_attn(const void *q, const void *k, const void *k_scales,
       part_o = (float *)ws;
       part_ml = part_o + (size_t)splits * rows * AT_D;
     }
-    int r = launch_attn_tc((const uint16_t *)q, (const uint16_t *)k, (const uint16_t *)v, parents,
+    int r = launch_attn_tc(kv_format, (const uint16_t *)q, k, k_scales, k_biases, v, v_scales, v_biases, parents,
                            (const unsigned long long *)bits, B, T, Hq, Hkv, n_kv, tail, kv_capacity, scale,
                            (uint16_t *)out, lse, part_o, part_ml, st);
     if (r != TSB_OK) return r;

@@ -95,6 +95,12 @@ def _full_case(bsz, L, fmt, seed, t=32, hq=24, hkv=4, d=256, heads_checked=(0, 1
         kb, vb = kf.to(torch.bfloat16), vf.to(torch.bfloat16)
         cache = tsb.KVCache(kb, vb, n_kv)
         kval, vval = kb.float(), vb.float()
+    elif fmt == "ref_q8":
+        kq, ksc = tsb.quantize_rows(kf)
+        vq, vsc = tsb.quantize_rows(vf)
+        cache = tsb.Q8KVCache(kq, vq, ksc, vsc, n_kv)
+        kval = torch.from_numpy(kv.dequant_rows(kq.cpu().numpy(), ksc.cpu().numpy())).float()
+        vval = torch.from_numpy(kv.dequant_rows(vq.cpu().numpy(), vsc.cpu().numpy())).float()
     else:
         kw, ks, kbias = tsb.quantize_g64(kf)
         vw, vs, vbias = tsb.quantize_g64(vf)
@@ -123,9 +129,86 @@ def test_attn_config4_bf16(bsz, L):
     _full_case(bsz, L, "bf16", seed=100 + bsz + L)
 
 
-@pytest.mark.parametrize("bsz,L", [(1, 1024), (4, 8192)])
+@pytest.mark.parametrize("bsz,L", [(1, 1024), (4, 8192), (1, 32768)])
 def test_attn_config4_mlx_q8(bsz, L):
     _full_case(bsz, L, "mlx_q8", seed=200 + bsz + L)
+
+
+@pytest.mark.parametrize("bsz,L", [(1, 1024), (4, 8192), (1, 32768)])
+def test_attn_config4_ref_q8(bsz, L):
+    _full_case(bsz, L, "ref_q8", seed=300 + bsz + L)
+
+
+def _cache_with_tail_rows(fmt, n_kv, cap, fill, seed, bsz=2, hkv=4, d=256):
+    """A cache whose rows >= n_kv hold `fill` (bf16 values, or the 8-bit
+    formats' scales); rows < n_kv are the same for every fill."""
+    import tsb
+
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kf = torch.randn(bsz, hkv, cap, d, device="cuda", generator=g)
+    vf = torch.randn(bsz, hkv, cap, d, device="cuda", generator=g)
+    if fmt == "bf16":
+        kb, vb = kf.to(torch.bfloat16), vf.to(torch.bfloat16)
+        kb[:, :, n_kv:] = fill
+        vb[:, :, n_kv:] = fill
+        return tsb.KVCache(kb, vb, n_kv)
+    if fmt == "ref_q8":
+        kq, ksc = tsb.quantize_rows(kf)
+        vq, vsc = tsb.quantize_rows(vf)
+        ksc[:, :, n_kv:] = fill
+        vsc[:, :, n_kv:] = fill
+        return tsb.Q8KVCache(kq, vq, ksc, vsc, n_kv)
+    kw, ks, kbias = tsb.quantize_g64(kf)
+    vw, vs, vbias = tsb.quantize_g64(vf)
+    for t in (ks, kbias, vs, vbias):
+        t[:, :, n_kv:] = fill
+    return tsb.MLXQ8KVCache(kw, vw, ks, kbias, vs, vbias, n_kv)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "ref_q8", "mlx_q8"])
+@pytest.mark.parametrize("n_kv", [1000, 1024 + 7])
+def test_attn_rows_past_n_kv_never_read_into_output(fmt, n_kv):
+    """Cache rows at or past n_kv (here NaN, inside the same tile as the last
+    keys) leave the output bit-identical to a cache with zeros there."""
+    import tsb
+
+    cap = n_kv + 40
+    t, hq = 16, 24
+    q = torch.randn(2, hq, t, 256, device="cuda").to(torch.bfloat16)
+    rng = np.random.default_rng(n_kv)
+    parents = dev(np.stack([gen.tree_parents(rng, t) for _ in range(2)]))
+    outs = []
+    for fill in (0.0, float("nan")):
+        cache = _cache_with_tail_rows(fmt, n_kv, cap, fill, seed=n_kv)
+        outs.append(tsb.tree_flash(q, cache, 256**-0.5, parents=parents))
+    torch.cuda.synchronize()
+    assert not torch.isnan(outs[1].float()).any()
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_attn_mlx_q8_odd_capacity():
+    """MLX 8-bit caches with an odd capacity take the warp-MMA kernel; the
+    results meet the same bar."""
+    import tsb
+
+    torch.manual_seed(7)
+    t, hq, hkv, d, n_kv = 8, 24, 4, 256, 700
+    cap = 701
+    kf = torch.randn(1, hkv, cap, d, device="cuda")
+    vf = torch.randn(1, hkv, cap, d, device="cuda")
+    q = torch.randn(1, hq, t, d, device="cuda").to(torch.bfloat16)
+    kw, ks, kbias = tsb.quantize_g64(kf)
+    vw, vs, vbias = tsb.quantize_g64(vf)
+    cache = tsb.MLXQ8KVCache(kw, vw, ks, kbias, vs, vbias, n_kv)
+    rng = np.random.default_rng(7)
+    parents = gen.tree_parents(rng, t)[None]
+    out = tsb.tree_flash(q, cache, d**-0.5, parents=dev(parents))
+    torch.cuda.synchronize()
+    kval = kv.dequant_g64(kw.cpu().numpy().view(np.uint32), bf16.from_torch_bf16(ks), bf16.from_torch_bf16(kbias))
+    vval = kv.dequant_g64(vw.cpu().numpy().view(np.uint32), bf16.from_torch_bf16(vs), bf16.from_torch_bf16(vbias))
+    bits = tree.ancestor_bits_u64(parents[0])[None]
+    ref = attention.tree_attention(host_f32(q), kval, vval, n_kv, t, bits, d**-0.5)
+    assert_close_rel(host_f32(out), ref, 2e-2, "odd capacity")
 
 
 def test_attn_declines():
