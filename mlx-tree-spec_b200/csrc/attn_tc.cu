@@ -15,7 +15,7 @@
 //   warp 6     bf16: TMA of V tiles through a four-stage ring. K and V have
 //              their own producers so a K load never queues behind a V slot
 //              that waits for O += P V.
-//   warps 6-9  8-bit: convert each raw tile into the same swizzled bf16 tile
+//   warps 6-13 8-bit: convert each raw tile into the same swizzled bf16 tile
 //              the MMAs read (two-stage K and V rings): MLX s*q + b rounded to
 //              bf16 (as mlx dequantize), reference int8 exact in bf16 with its
 //              row scales applied outside the matmuls (tree_flash.py:14-19,
@@ -55,6 +55,7 @@ constexpr uint32_t TC_O = 0, TC_Q = 256, TC_S0 = 384;
 constexpr float TC_RESCALE_LOG2 = 8.f;
 constexpr int TC_RAW_CODES = TC_KT * TC_D;      // 16 KB: one tile of 8-bit codes
 constexpr int TC_NSC = 8;                       // reference-format row-scale ring (tiles)
+constexpr int TC_NCONV = 8;                     // converter warps (8-bit formats): two per SM sub-partition
 constexpr int TC_MAX_SMEM = 227 * 1024;
 
 template <int FMT>
@@ -72,7 +73,7 @@ struct TcCfg {
   static constexpr int SC_BYTES = REF ? TC_NSC * 2 * TC_KT * 4 : 0;
   static constexpr int NBARS = 2 + 2 * NK + 2 * NV + 8 + 2 * NR + (REF ? TC_NSC : 0);
   static constexpr int CTRL = Q8 ? 2048 : 1024;  // barriers, TMEM address, masks, parents
-  static constexpr int THREADS = Q8 ? 320 : 224;
+  static constexpr int THREADS = Q8 ? (6 + TC_NCONV) * 32 : 224;
   static constexpr size_t SMEM = (size_t)(NK + NV) * TC_KV_BYTES + (size_t)NR * RAW_STAGE + SC_BYTES + CTRL + 1024;
   static_assert((NBARS + 1) * 8 + 64 * 8 + 64 * 4 <= CTRL, "control block");
   static_assert(SMEM <= TC_MAX_SMEM, "shared memory");
@@ -110,9 +111,9 @@ TSB_HD uint64_t desc_mnmajor_sw128(uint32_t smem_byte_addr, uint32_t lbo) {
   return d;
 }
 
-// Byte k of w as float 2^23 + byte (exact): the byte becomes the low mantissa
-// byte of 0x4B000000.
-TSB_HD float byte_f32_2p23(uint32_t w, uint32_t k) { return __uint_as_float(prmt(w, 0x4B000000u, 0x7540u | k)); }
+// Byte k of w as the bits of float 2^23 + byte (exact): the byte becomes the
+// low mantissa byte of 0x4B000000.
+TSB_HD uint32_t byte_2p23(uint32_t w, uint32_t k) { return prmt(w, 0x4B000000u, 0x7540u | k); }
 
 // 8 MLX codes (u8, low byte first) -> 8 bf16 of s*q + b: q exact in float,
 // one float fma, round to nearest even (the dequantization of mlx
@@ -124,8 +125,8 @@ TSB_HD uint4 dequant8_mlx(uint2 w, float s, float b) {
   for (int h = 0; h < 2; ++h) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const float q0 = byte_f32_2p23(ws[h], 2 * e) - 8388608.f;
-      const float q1 = byte_f32_2p23(ws[h], 2 * e + 1) - 8388608.f;
+      const float q0 = __uint_as_float(byte_2p23(ws[h], 2 * e)) - 8388608.f;
+      const float q1 = __uint_as_float(byte_2p23(ws[h], 2 * e + 1)) - 8388608.f;
       o[2 * h + e] = pack_bf16x2(__fmaf_rn(q0, s, b), __fmaf_rn(q1, s, b));
     }
   }
@@ -141,8 +142,8 @@ TSB_HD uint4 convert8_s8(uint2 w) {
   for (int h = 0; h < 2; ++h) {
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const float q0 = byte_f32_2p23(ws[h], 2 * e) - 8388736.f;  // 2^23 + 128
-      const float q1 = byte_f32_2p23(ws[h], 2 * e + 1) - 8388736.f;
+      const float q0 = __uint_as_float(byte_2p23(ws[h], 2 * e)) - 8388736.f;  // 2^23 + 128
+      const float q1 = __uint_as_float(byte_2p23(ws[h], 2 * e + 1)) - 8388736.f;
       o[2 * h + e] = pack_bf16x2(q0, q1);
     }
   }
@@ -191,8 +192,8 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
   const int tail_lo = a.n_kv - a.tail;
 
   if (threadIdx.x == 0) {
-    // bf16 tiles are filled by a TMA transaction, 8-bit ones by the four converter warps
-    const uint32_t fill = C::Q8 ? 4 : 1;
+    // bf16 tiles are filled by a TMA transaction, 8-bit ones by the converter warps
+    const uint32_t fill = C::Q8 ? TC_NCONV : 1;
     mbar_init(q_full, 1);
     mbar_init(q_done, 4);
     for (int i = 0; i < NK; ++i) { mbar_init(&k_full[i], fill); mbar_init(&k_free[i], 1); }
@@ -203,9 +204,9 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
     }
-    for (int i = 0; i < NR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_free[i], 4); }
+    for (int i = 0; i < NR; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_free[i], TC_NCONV); }
     if (C::REF)
-      for (int i = 0; i < TC_NSC; ++i) mbar_init(&sc_full[i], 4);
+      for (int i = 0; i < TC_NSC; ++i) mbar_init(&sc_full[i], TC_NCONV);
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -231,7 +232,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       mbar_arrive_expect_tx(q_full, TC_Q_BYTES);
 #pragma unroll
       for (int d = 0; d < 4; ++d) tma_load_2d(sQ + d * TC_QBOX, &tmap_q, d * 64, qrow, q_full);
-      if (!C::Q8) {
+      if constexpr (!C::Q8) {
         bool ok = true;
         int j = 0;
         for (; j < nt && ok; ++j) {
@@ -294,8 +295,9 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         }
       }
     }
-  } else if (!C::Q8 && warp == 6) {
-    // ---------------- V producer (bf16)
+  } else if (warp >= 6) {
+    if constexpr (!C::Q8) {
+    // ---------------- V producer (bf16; warp 6 is the last warp)
     if (elect_one()) {
       bool ok = true;
       int j = 0;
@@ -316,13 +318,13 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
         }
       }
     }
-  } else if (C::Q8 && warp >= 6) {
-    // ---------------- converters (8-bit): raw tile -> swizzled bf16 tile
+    } else {
+    // ---------------- converters (8-bit, warps 6-13): raw tile -> swizzled bf16 tile
     // Thread (warp w, lane l) writes 16-byte chunk l&7 of D box l>>3 (the MLX
-    // group) of rows (w-6) + 4i: eight lanes fill one 128-byte row of a box.
+    // group) of rows (w-6) + 8i: eight lanes fill one 128-byte row of a box.
     const int r_lo = warp - 6;
     const int grp = lane >> 3, ch = lane & 7;
-    const int ct = threadIdx.x - 192;  // 0..127
+    const int ct = threadIdx.x - 192;  // 0 .. 32 * TC_NCONV - 1
     int seq = 0;
     auto convert = [&](bool isv, int j) -> bool {
       const int rs = seq % NR;
@@ -345,27 +347,50 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       // reference format: the tile's key (threads 0-63) and value (64-127) row
       // scales, fetched with the K tile, for the softmax warps
       float rsc = 0.f;
-      if (C::REF && !isv) {
+      if (C::REF && !isv && ct < 2 * TC_KT) {
         const int r = ct & 63;
         if (r < nvalid) rsc = reinterpret_cast<const float *>(ct < 64 ? a.ks : a.vs)[kv_row0 + key0 + r];
       }
       if (!warp_wait(&raw_full[rs], (seq / NR) & 1)) return false;
       const unsigned char *raw = sRaw + rs * C::RAW_STAGE;
       const uint16_t *rsb = reinterpret_cast<const uint16_t *>(raw + TC_RAW_CODES);
-#pragma unroll 4
-      for (int i = 0; i < TC_KT / 4; ++i) {
-        const int r = r_lo + 4 * i;
-        uint4 o = make_uint4(0u, 0u, 0u, 0u);
-        if (r < nvalid) {
-          const uint2 w = *reinterpret_cast<const uint2 *>(raw + r * TC_D + lane * 8);
-          if (C::MLX)
-            o = dequant8_mlx(w, bf16_bits_to_float(rsb[r * 4 + grp]), bf16_bits_to_float(rsb[TC_KT * 4 + r * 4 + grp]));
-          else
-            o = convert8_s8(w);
+      // batches of CB rows: all loads of a batch first, then the conversions
+      // and stores; the batch loop stays rolled (the instruction cache holds
+      // the converter and softmax loops of the same sub-partition)
+      constexpr int CB = 4, ROWS = TC_KT / TC_NCONV;
+      static_assert(TC_KT % TC_NCONV == 0 && ROWS % CB == 0, "converter rows");
+#pragma unroll 1
+      for (int h = 0; h < ROWS / CB; ++h) {
+        uint2 w[CB];
+        uint32_t sb[CB], bb[CB];
+#pragma unroll
+        for (int i = 0; i < CB; ++i) {
+          const int r = r_lo + TC_NCONV * (CB * h + i);
+          w[i] = make_uint2(0u, 0u);
+          sb[i] = 0u;
+          bb[i] = 0u;
+          if (r < nvalid) {
+            w[i] = *reinterpret_cast<const uint2 *>(raw + r * TC_D + lane * 8);
+            if (C::MLX) {
+              sb[i] = rsb[r * 4 + grp];
+              bb[i] = rsb[TC_KT * 4 + r * 4 + grp];
+            }
+          }
         }
-        *reinterpret_cast<uint4 *>(dst + grp * TC_KVBOX + r * 128 + ((ch ^ (r & 7)) << 4)) = o;
+#pragma unroll
+        for (int i = 0; i < CB; ++i) {
+          const int r = r_lo + TC_NCONV * (CB * h + i);
+          uint4 o = make_uint4(0u, 0u, 0u, 0u);
+          if (r < nvalid) {
+            if (C::MLX)
+              o = dequant8_mlx(w[i], __uint_as_float(sb[i] << 16), __uint_as_float(bb[i] << 16));
+            else
+              o = convert8_s8(w[i]);
+          }
+          *reinterpret_cast<uint4 *>(dst + grp * TC_KVBOX + r * 128 + ((ch ^ (r & 7)) << 4)) = o;
+        }
       }
-      if (C::REF && !isv) sSc[(j % TC_NSC) * 2 * TC_KT + ct] = rsc;
+      if (C::REF && !isv && ct < 2 * TC_KT) sSc[(j % TC_NSC) * 2 * TC_KT + ct] = rsc;
       fence_proxy_async_smem();  // generic writes -> MMA reads; raw slot reads -> TMA refill
       __syncwarp();
       if (lane == 0) {
@@ -381,6 +406,7 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
       if (j == 0) ok = convert(false, 0);
       if (ok && j + 1 < nt) ok = convert(false, j + 1);
       if (ok) ok = convert(true, j);
+    }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
