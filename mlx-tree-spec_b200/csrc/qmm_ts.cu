@@ -11,8 +11,11 @@
 // 4 bytes of shared-memory traffic per weight; tcgen05.st into TMEM keeps the
 // shared-memory path for the packed codes and x only.
 //
-// Schedule: a persistent, stream-K grid of P <= #SM co-resident CTAs (one per
-// SM: all 512 TMEM columns). The work is the list of (row tile of 128 weight
+// Schedule: a persistent, stream-K grid of P <= #SM CTAs (one per SM: all 512
+// TMEM columns), launched as a programmatic dependent of the previous kernel on
+// the stream: CTAs start as that kernel's CTAs exit and stream the (constant)
+// weights at once; x, y and the workspace wait for the previous grid to
+// complete (griddepcontrol.wait). The work is the list of (row tile of 128 weight
 // rows, stage of 4 groups = 256 K) units, tile-major; CTA c takes the
 // contiguous units [U c / P, U (c+1) / P). Its range crosses tile boundaries,
 // so it works on a sequence of tile segments. A segment that covers a whole
@@ -187,6 +190,9 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   };
 
   if (threadIdx.x == 0) {
+    // the next kernel on the stream may start its CTAs as this one's exit (it
+    // waits for this grid before touching anything this grid writes)
+    griddep_launch_dependents();
     for (int s = 0; s < C::NC; ++s) {
       mbar_init(&full_c[s], 1);
       mbar_init(&free_c[s], 4);  // the 4 warps of the stage's warpgroup
@@ -237,6 +243,9 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
       int issued = 0;
       int tile, st;
       unit(0, tile, st);
+      // x may be the previous kernel's output; the weights, scales and biases
+      // are constant, so their stream starts before that kernel has finished
+      if (!codes) griddep_wait();
       for (int li = 0; li < L; ++li, ring.next(nslots), step(tile, st, 1)) {
         if (li >= nslots && !mbar_wait(&freed[ring.slot], ring.phase ^ 1u)) break;
         const int gs = st * C::SG;
@@ -358,40 +367,38 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         const uint2 bv = *reinterpret_cast<const uint2 *>(cb + C::C_BYTES + C::SB_BYTES + off);
         s_w[0] = sv.x; s_w[1] = sv.y; b_w[0] = bv.x; b_w[1] = bv.y;
       }
-      // the stage's 32 packed words of this row, then release the codes slot
-      uint32_t words[32];
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        const int chunk = cc ^ (r & 7);  // TMA 128-byte swizzle
-        const uint4 v = *reinterpret_cast<const uint4 *>(cb + r * 128 + chunk * 16);
-        words[4 * cc + 0] = v.x; words[4 * cc + 1] = v.y; words[4 * cc + 2] = v.z; words[4 * cc + 3] = v.w;
-      }
-      // the slot is refilled by TMA (async proxy): order these generic-proxy reads
-      // before that write, which the mbarrier release alone does not do
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&free_c[cs]);
       // the A slot is free once the MMAs of this warpgroup's previous stage completed
       if (ai > 0 && !warp_wait(&a_empty[wg], (uint32_t)((ai - 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
-#pragma unroll
-      for (int gl = 0; gl < C::SG; ++gl) {
-        if (gl >= ng) break;
-        const uint32_t sb = (s_w[gl >> 1] >> (16 * (gl & 1))) & 0xFFFFu;
-        const uint32_t bb = (b_w[gl >> 1] >> (16 * (gl & 1))) & 0xFFFFu;
+      // one group at a time (a rolled loop keeps this role's code small next to
+      // the other roles sharing the sub-partition's instruction cache): its
+      // eight packed words, dequantized into 32 TMEM columns
+      const uint64_t s64 = ((uint64_t)s_w[1] << 32) | s_w[0], b64 = ((uint64_t)b_w[1] << 32) | b_w[0];
+#pragma unroll 1
+      for (int gl = 0; gl < ng; ++gl) {
+        const uint4 v0 = *reinterpret_cast<const uint4 *>(cb + r * 128 + (((2 * gl) ^ (r & 7)) << 4));
+        const uint4 v1 = *reinterpret_cast<const uint4 *>(cb + r * 128 + (((2 * gl + 1) ^ (r & 7)) << 4));
+        const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const uint32_t sb = (uint32_t)(s64 >> (16 * gl)) & 0xFFFFu;
+        const uint32_t bb = (uint32_t)(b64 >> (16 * gl)) & 0xFFFFu;
         const __nv_bfloat162 s2 = u32_as_bf2(sb | (sb << 16));
         const __nv_bfloat162 b2 = u32_as_bf2(bb | (bb << 16));
 #pragma unroll
         for (int wj = 0; wj < 8; ++wj) {
           uint32_t o[4];
-          dequant_word(words[gl * 8 + wj], s2, b2, o);
+          dequant_word(words[wj], s2, b2, o);
           wt[4 * wj + 0] = o[0]; wt[4 * wj + 1] = o[1]; wt[4 * wj + 2] = o[2]; wt[4 * wj + 3] = o[3];
         }
         tmem_st32(lane_base + C::A_COL0 + (wg * C::SG + gl) * C::GA, wt);
       }
+      // the codes slot is refilled by TMA (async proxy): order these generic-proxy
+      // reads before that write, which the mbarrier release alone does not do
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&free_c[cs]);
       // tcgen05.st reads its source registers at issue (wt is reused above); the
       // stores must only have reached TMEM before the issuers are told
       tmem_wait_st();
@@ -408,6 +415,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     const int q = warp;
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    griddep_wait();  // y and the workspace flags/partials are shared with the previous call
     int li = 0, seg = 0;
     int tile, st0;
     unit(0, tile, st0);
@@ -625,11 +633,14 @@ int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uin
   cfg.blockDim = dim3(C::THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
-  // the first part of a split tile waits for the later parts: all CTAs must be
-  // co-resident (P <= #SM, one CTA per SM), which a cooperative launch guarantees
+  // Programmatic dependent launch: CTAs start on SMs as the previous kernel's
+  // CTAs exit, and stream weights while it finishes. The first part of a split
+  // tile waits for the later parts, which become resident as SMs free up (P <=
+  // #SM, one CTA per SM; the previous kernel never waits on this one), so every
+  // wait ends; a cooperative launch would hold the grid until all SMs are free.
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_ts_kernel<NP>, tx, tw, tsc, tbi, a);

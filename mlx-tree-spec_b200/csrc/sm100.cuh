@@ -99,6 +99,14 @@ TSB_HD bool warp_wait(uint64_t *bar, uint32_t parity) {
 TSB_HD void named_barrier_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
 TSB_HD void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Let the next kernel of the stream (launched with programmatic stream
+// serialization) schedule its CTAs as this grid's CTAs exit.
+TSB_HD void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Block until the previous grid of the stream has completed and its writes are
+// visible (returns at once for a kernel launched without the attribute).
+TSB_HD void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 TSB_HD void tma_prefetch_desc(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
