@@ -11,8 +11,9 @@ quantized); weights rotate through a pool of copies much larger than L2, so
 no call reads another call's weights from L2.
 
 At N > 1 GPUs (one process per GPU, torchrun) every weight is N-sharded by
-output rows and each layer's output is reassembled with an NCCL all-gather over
-NVLink inside the timed region (total work fixed: strong scaling).
+output rows and each layer's output is reassembled on every GPU inside the
+timed region by the qmm kernel itself, which stores its columns into every
+rank's output over NVLink (total work fixed: strong scaling).
 
 `--impl reference` times the reference's algorithm on the host CPU (the oracle
 port: dequantize + float32 matmul over all host threads; the reference's own
@@ -241,8 +242,13 @@ def run_tsb(args):
     gen = torch.Generator(device="cuda").manual_seed(7)
     xs = {(m, k): torch.randn(m, k, device="cuda", generator=gen).to(torch.bfloat16)
           for m in SWEEP_M for k in {k for _, k in SHAPES}}
-    sharded = tdist.ShardedQMM(world, rank) if world > 1 else None
-    ys = {(m, n): torch.empty(m, n, dtype=torch.bfloat16, device="cuda") for (m, n, k) in calls}
+    # N > 1: the output of every call is gathered inside the qmm kernel (peer
+    # stores into every rank's y over NVLink); no separate collective
+    sharded = tdist.GatheredQMM(world, rank) if world > 1 else None
+    if sharded is None:
+        ys = {(m, n): torch.empty(m, n, dtype=torch.bfloat16, device="cuda") for (m, n, k) in calls}
+    else:
+        ys = {(m, n): sharded.out_buffer(m, n) for (m, n, k) in calls}
 
     def launch(m, n, k, copy, y=None):
         wq, s, b = pool.shards[(n, k)][copy % len(pool.shards[(n, k)])]
@@ -395,7 +401,8 @@ def run_tsb(args):
                                    "{(6144,5120),(34816,5120),(5120,17408)}, 4-bit g64 MLX format",
                        "bytes_per_step": total_bytes, "calls_per_step": len(calls),
                        "l2": "inputs larger than L2: rotating weight pool, >= 2.5 x 126 MiB of distinct copies per shape",
-                       "parallelism": f"N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "parallelism": (f"N-shard x{world}, output gathered inside the qmm kernel (peer stores "
+                                       "over NVLink)") if world > 1 else "single GPU",
                        "timing": "CUDA graph of one step, CUDA events"},
             "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms, 4), "path": "tsb.quantized_matmul, pinned host x/y, eager"},

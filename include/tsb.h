@@ -96,6 +96,38 @@ size_t tsb_qmm_workspace_bytes(int M, int N, int K);
 int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const void *biases, void *y,
                   int M, int N, int K, int ldy, void *ws, size_t ws_bytes, tsb_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * N-sharded quantized matmul with the output gathered over the GPUs of one
+ * node inside the same kernel. The reference runs on one device; this is the
+ * tensor-parallel form of tsb_qmm_w4g64 (the layer's full output on every GPU,
+ * as an N-split matmul followed by an all-gather would leave it).
+ *
+ * Rank `rank` of `world` holds rows [rank*Ns, (rank+1)*Ns) of W (itself a
+ * valid MLX-format weight of Ns rows) and computes columns [rank*Ns,
+ * (rank+1)*Ns) of y. Its kernel stores that slice into every rank's y (peer
+ * stores over NVLink), so when the call completes on a rank's stream, that
+ * rank's y [M, ldy] holds all world*Ns columns.
+ *   y[p]    rank p's output buffer, mapped into this process (peer memory);
+ *           the same [M, ldy] layout on every rank
+ *   sig[p]  rank p's signal block, mapped likewise: 2*world + 3 uint32,
+ *           zero-filled once before the first call, then owned by these calls
+ * Every rank makes the same sequence of calls with the same block (one block
+ * per stream of calls); a rank that stops leaves its peers' calls to end in
+ * TSB_ETIMEOUT (tsb_device_status). Before storing into a peer's y, a call
+ * waits until that peer has started the same call, so work queued before it
+ * on the peer's stream (readers of the old contents) has finished.
+ * M <= 128 (the verify path; larger M: TSB_EUNSUPPORTED), ldy >= world*Ns;
+ * workspace tsb_qmm_workspace_bytes(M, Ns, K); other rules as tsb_qmm_w4g64.
+ * ---------------------------------------------------------------------- */
+#define TSB_MAX_GATHER_RANKS 8
+typedef struct {
+  int world, rank;
+  void *y[TSB_MAX_GATHER_RANKS];
+  uint32_t *sig[TSB_MAX_GATHER_RANKS];
+} tsb_gather_t;
+int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void *scales, const void *biases, int M, int Ns,
+                         int K, int ldy, const tsb_gather_t *g, void *ws, size_t ws_bytes, tsb_stream_t stream);
+
 /* Bit-exact dequantization: out[n, k] = bf16_rne(fmaf(q, s, b)) as bf16 [N, K].
  * Reference rule: `T(float(q) * s + b)` in qmm_packed.py:200,348,635.
  * Requirements: K % 64 == 0. */

@@ -24,6 +24,15 @@ static inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Peers of a gathered output (tsb_gather_t after checks): the kernel stores
+// this rank's columns [col0, col0 + N) into y[p] for every rank p.
+constexpr int kMaxGatherRanks = TSB_MAX_GATHER_RANKS;
+struct GatherSpec {
+  int world, rank, col0;
+  void *y[kMaxGatherRanks];
+  uint32_t *sig[kMaxGatherRanks];
+};
+
 TSB_HD float bf16_bits_to_float(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
 
 TSB_HD float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }

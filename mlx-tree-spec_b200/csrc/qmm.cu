@@ -5,7 +5,7 @@
 
 namespace tsb {
 int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-           int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st);
+           int K, int ldy, void *ws, size_t ws_bytes, const GatherSpec *gs, cudaStream_t st);
 size_t qmm_ts_workspace_bytes(int M, int N, int K);
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
              int K, int ldy, cudaStream_t st);
@@ -34,7 +34,36 @@ extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scale
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16)) return TSB_EINVAL;
   if (M <= kTsMaxRows)
     return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
-                  ldy, ws, ws_bytes, (cudaStream_t)stream);
+                  ldy, ws, ws_bytes, nullptr, (cudaStream_t)stream);
   return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
                   ldy, (cudaStream_t)stream);
+}
+
+// Tensor-parallel form: this rank's N-shard, its output columns stored into
+// every rank's y by the kernel itself (no separate all-gather).
+extern "C" int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void *scales, const void *biases, int M,
+                                    int Ns, int K, int ldy, const tsb_gather_t *g, void *ws, size_t ws_bytes,
+                                    tsb_stream_t stream) {
+  if (!x || !w || !scales || !biases || !g) return TSB_EINVAL;
+  if (g->world < 1 || g->world > TSB_MAX_GATHER_RANKS || g->rank < 0 || g->rank >= g->world) return TSB_EINVAL;
+  if (M <= 0 || Ns <= 0 || K <= 0) return TSB_EINVAL;
+  if (K % 64 || Ns % 128) return TSB_EUNSUPPORTED;
+  if (M > kTsMaxRows) return TSB_EUNSUPPORTED;
+  if ((long long)ldy < (long long)Ns * g->world || ldy % 8) return TSB_EINVAL;
+  if (!aligned(x, 16) || !aligned(w, 16)) return TSB_EINVAL;
+  GatherSpec gs;
+  gs.world = g->world;
+  gs.rank = g->rank;
+  gs.col0 = g->rank * Ns;
+  for (int p = 0; p < kMaxGatherRanks; ++p) {
+    gs.y[p] = nullptr;
+    gs.sig[p] = nullptr;
+  }
+  for (int p = 0; p < g->world; ++p) {
+    if (!g->y[p] || !aligned(g->y[p], 16) || !g->sig[p] || !aligned(g->sig[p], 4)) return TSB_EINVAL;
+    gs.y[p] = g->y[p];
+    gs.sig[p] = g->sig[p];
+  }
+  return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases,
+                (uint16_t *)g->y[g->rank] + gs.col0, M, Ns, K, ldy, ws, ws_bytes, &gs, (cudaStream_t)stream);
 }

@@ -126,12 +126,47 @@ struct Part {
 
 struct TsArgs {
   const uint16_t *scales, *biases;
-  uint16_t *y;
   float *partials;     // [tiles][maxp][NP][128], part 0 unused
   uint32_t *flags;     // [tiles][maxp], zero between calls
   long long U;
   int M, N, K, ldy, P, nst, maxp;
+  // Output over `world` GPUs: yp[p] is rank p's y at this rank's first column
+  // (world 1: yp[0] is y). sig[p] is rank p's signal block: words [0, world)
+  // hold the epoch each rank last started; [world, 2 world) count the CTAs of
+  // each rank that have finished writing their part of y there (cumulative
+  // over calls); [2 world, 2 world + 3) are rank p's own counters (CTAs done
+  // in the current call, epoch, cumulative CTA total).
+  int world, rank;
+  uint16_t *yp[kMaxGatherRanks];
+  uint32_t *sig[kMaxGatherRanks];
 };
+
+TSB_HD uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+TSB_HD void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+TSB_HD void red_add_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until every other rank's word `base + p` has reached value ep
+// (wrap-safe comparison); false (and TSB_ETIMEOUT recorded) if one does not.
+TSB_HD bool wait_peers(const uint32_t *base, int world, int rank, uint32_t ep) {
+  for (int p = 0; p < world; ++p) {
+    if (p == rank) continue;
+    const unsigned long long t0 = globaltimer_ns();
+    while ((int)(ld_acquire_sys(base + p) - ep) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_status(TSB_ETIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
 
 TSB_HD uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
@@ -416,6 +451,19 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     const int r = q * 32 + lane;
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
     griddep_wait();  // y and the workspace flags/partials are shared with the previous call
+    // Gather over GPUs: this call's epoch (the previous call has completed, so
+    // its epoch is final). CTA 0 tells every peer that this rank has started
+    // it, i.e. that everything before it on this rank's stream (the readers of
+    // the previous contents of y) has finished; remote stores into a peer's y
+    // wait for that peer's word (once, before this CTA's first y store).
+    uint32_t ep = 0;
+    bool peers_started = a.world == 1;
+    if (a.world > 1) {
+      ep = *reinterpret_cast<volatile uint32_t *>(a.sig[a.rank] + 2 * a.world + 1) + 1u;
+      if (c == 0 && threadIdx.x == 0)
+        for (int pp = 0; pp < a.world; ++pp)
+          if (pp != a.rank) st_release_sys(a.sig[pp] + a.rank, ep);
+    }
     int li = 0, seg = 0;
     int tile, st0;
     unit(0, tile, st0);
@@ -518,9 +566,17 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
               }
           }
         }
+        if (!peers_started) {
+          if (threadIdx.x == 0) wait_peers(a.sig[a.rank], a.world, a.rank, ep);
+          named_barrier_sync(1, 128);
+          peers_started = true;
+        }
 #pragma unroll
         for (int e = 0; e < CW; ++e)
-          if (c0 + e < a.M) a.y[(size_t)(c0 + e) * a.ldy + row] = float_to_bf16_bits(v[e]);
+          if (c0 + e < a.M) {
+            const uint16_t h = float_to_bf16_bits(v[e]);
+            for (int pp = 0; pp < a.world; ++pp) a.yp[pp][(size_t)(c0 + e) * a.ldy + row] = h;
+          }
       }
       // the accumulators are read: the issuers may start the next segment
       tc_fence_before();
@@ -547,6 +603,25 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (a.world > 1 && threadIdx.x == 0) {
+    // Every CTA counts itself done in each peer's block with a system-scope
+    // release (cumulative: it orders this CTA's peer stores, which the barrier
+    // above ordered before it); the CTAs release in parallel as they finish.
+    // The last CTA of this rank then waits until every peer's count has
+    // reached this rank's own running total (every rank makes the same calls
+    // with the same grid), so y is complete on every rank when the grid
+    // completes.
+    uint32_t *own = a.sig[a.rank];
+    for (int pp = 0; pp < a.world; ++pp)
+      if (pp != a.rank) red_add_release_sys(a.sig[pp] + a.world + a.rank, 1u);
+    if (atomicAdd(own + 2 * a.world, 1u) + 1u == gridDim.x) {
+      own[2 * a.world] = 0u;
+      const uint32_t total = own[2 * a.world + 2] + gridDim.x;
+      wait_peers(own + a.world, a.world, a.rank, total);
+      own[2 * a.world + 2] = total;
+      own[2 * a.world + 1] += 1u;  // this call's epoch is complete on this rank
+    }
   }
 }
 
@@ -583,7 +658,7 @@ TsPlan plan_ts(int M, int N, int K) {
 
 template <int NP>
 int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-              int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st) {
+              int K, int ldy, void *ws, size_t ws_bytes, const GatherSpec *gs, cudaStream_t st) {
   using C = TsCfg<NP>;
   const TsPlan plan = plan_ts<NP>(M, N, K);
   if ((size_t)plan.tiles * plan.maxp * sizeof(uint32_t) > kFlagRegionBytes) return TSB_EUNSUPPORTED;
@@ -620,7 +695,19 @@ int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uin
   TsArgs a;
   a.scales = s;
   a.biases = b;
-  a.y = y;
+  if (gs) {
+    a.world = gs->world;
+    a.rank = gs->rank;
+    for (int p = 0; p < kMaxGatherRanks; ++p) {
+      a.yp[p] = p < gs->world ? static_cast<uint16_t *>(gs->y[p]) + gs->col0 : nullptr;
+      a.sig[p] = p < gs->world ? static_cast<uint32_t *>(gs->sig[p]) : nullptr;
+    }
+  } else {
+    a.world = 1;
+    a.rank = 0;
+    for (int p = 0; p < kMaxGatherRanks; ++p) { a.yp[p] = nullptr; a.sig[p] = nullptr; }
+    a.yp[0] = y;
+  }
   a.flags = static_cast<uint32_t *>(ws);
   a.partials = reinterpret_cast<float *>(static_cast<unsigned char *>(ws) + plan.flag_bytes);
   a.U = plan.U;
@@ -662,11 +749,11 @@ size_t qmm_ts_workspace_bytes(int M, int N, int K) {
 
 // M in [1, 128]: tokens padded to a multiple of 16 for the MMA's N.
 int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-           int K, int ldy, void *ws, size_t ws_bytes, cudaStream_t st) {
-  if (M <= 16) return launch_ts<16>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
-  if (M <= 32) return launch_ts<32>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
-  if (M <= 64) return launch_ts<64>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
-  return launch_ts<128>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, st);
+           int K, int ldy, void *ws, size_t ws_bytes, const GatherSpec *gs, cudaStream_t st) {
+  if (M <= 16) return launch_ts<16>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
+  if (M <= 32) return launch_ts<32>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
+  if (M <= 64) return launch_ts<64>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
+  return launch_ts<128>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
 }
 
 unsigned int status_ts(bool reset) {

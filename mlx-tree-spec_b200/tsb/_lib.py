@@ -24,6 +24,17 @@ TSB_KV_BF16 = 0
 TSB_KV_MLX_Q8_G64 = 1
 TSB_KV_REF_Q8_ROW = 2
 
+TSB_MAX_GATHER_RANKS = 8
+
+
+class GatherT(ctypes.Structure):
+    """tsb_gather_t: each rank's output buffer and signal block, as mapped here."""
+
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int),
+                ("y", ctypes.c_void_p * TSB_MAX_GATHER_RANKS),
+                ("sig", ctypes.c_void_p * TSB_MAX_GATHER_RANKS)]
+
+
 # Every symbol include/tsb.h declares, with (restype, argtypes).
 _P, _I, _Z, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_float
 SIGNATURES = {
@@ -32,6 +43,7 @@ SIGNATURES = {
     "tsb_device_status": (_I, [_P, _I]),
     "tsb_qmm_workspace_bytes": (_Z, [_I, _I, _I]),
     "tsb_qmm_w4g64": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "tsb_qmm_w4g64_gather": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(GatherT), _P, _Z, _P]),
     "tsb_dequant_w4g64": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "tsb_tree_ancestor_bits": (_I, [_P, _I, _I, _P, _P, _P]),
     "tsb_tree_attn_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),

@@ -4,8 +4,16 @@ The reference runs on one device and has no collectives. The B200 build adds
 one strategy, per its target: every 4-bit weight (N, K) is split by output
 rows over G ranks (rank r holds rows [r*N/G, (r+1)*N/G) of w, scales and
 biases, so each shard is itself a valid MLX-format weight); x is replicated;
-each rank computes its (M, N/G) slice and, where a layer's full output is
-needed, the slices are reassembled with one NCCL all-gather over NVLink.
+each rank computes its (M, N/G) slice and every rank ends with the full
+(M, N) output.
+
+Two forms:
+  GatheredQMM  the verify path (M <= 128): one kernel per rank computes its
+               slice and stores it into every rank's output over NVLink (peer
+               memory from torch symmetric memory), exchanging completion
+               flags itself (tsb_qmm_w4g64_gather); no separate collective.
+  ShardedQMM   any M: the shard's matmul, then one NCCL all-gather and a
+               relayout into the caller's buffer.
 
 Every rank takes the same collective steps in the same order.
 """
@@ -76,5 +84,86 @@ class ShardedQMM:
         k = x.shape[-1]
         x2 = x.reshape(-1, k).contiguous()
         out = torch.empty(x2.shape[0], wq.shape[0] * self.world, dtype=x.dtype, device=x.device)
+        self.forward_into(x2, wq, s, b, out)
+        return out.reshape(*x.shape[:-1], out.shape[-1])
+
+
+# Words of a GatheredQMM signal block (the kernel uses 2 * world + 3 of them).
+SIG_WORDS = 64
+
+
+class GatheredQMM:
+    """y = x @ W.T with W N-sharded over the process group, gathered inside the
+    kernel: rank r's kernel writes its columns into every rank's y.
+
+    Outputs must come from out_buffer(m, n) (symmetric memory: every rank
+    holds the same buffer and can address its peers'). One signal block per
+    instance; every rank makes the same sequence of calls on one stream."""
+
+    def __init__(self, world: int, rank: int, group=None, device=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from . import _lib
+
+        if world > _lib.TSB_MAX_GATHER_RANKS:
+            raise ValueError(f"world {world} > {_lib.TSB_MAX_GATHER_RANKS}")
+        self.world, self.rank = world, rank
+        self.group = group if group is not None else dist.group.WORLD
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self._symm = symm_mem
+        sig = symm_mem.empty(SIG_WORDS, dtype=torch.int32, device=self.device)
+        sig.zero_()
+        self._sig = sig
+        self._sig_ptrs = list(symm_mem.rendezvous(sig, self.group).buffer_ptrs)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every block is zero before any rank's first call
+        self._outs: dict = {}
+
+    def out_buffer(self, m: int, n: int, dtype=torch.bfloat16) -> torch.Tensor:
+        """The (m, n) output buffer of this shape (allocated once, collectively:
+        every rank must ask for the same shapes in the same order)."""
+        key = (m, n, dtype)
+        hit = self._outs.get(key)
+        if hit is None:
+            from . import _lib
+
+            t = self._symm.empty(m, n, dtype=dtype, device=self.device)
+            ptrs = list(self._symm.rendezvous(t, self.group).buffer_ptrs)
+            g = _lib.GatherT()
+            g.world, g.rank = self.world, self.rank
+            for p in range(self.world):
+                g.y[p] = ptrs[p]
+                g.sig[p] = self._sig_ptrs[p]
+            hit = (t, g)
+            self._outs[key] = hit
+        return hit[0]
+
+    def forward_into(self, x, wq, s, b, out):
+        """x (M, K) contiguous; (wq, s, b) this rank's shard; out from out_buffer."""
+        import ctypes
+
+        from . import _lib
+        from .ops import _ptr, _stream, qmm_workspace
+
+        m, k = x.shape
+        ns = wq.shape[0]
+        hit = self._outs.get((out.shape[0], out.shape[1], out.dtype))
+        if hit is None or hit[0].data_ptr() != out.data_ptr():
+            raise ValueError("out must come from GatheredQMM.out_buffer")
+        lib = _lib.load()
+        ws = qmm_workspace(lib.tsb_qmm_workspace_bytes(m, ns, k), x.device)
+        st = lib.tsb_qmm_w4g64_gather(_ptr(x), _ptr(wq), _ptr(s), _ptr(b), m, ns, k, out.shape[1],
+                                      ctypes.byref(hit[1]), _ptr(ws), ws.numel(), _stream(x))
+        if st != _lib.TSB_OK:
+            raise _lib.TSBError(st, "tsb_qmm_w4g64_gather")
+        return out
+
+    def forward(self, x, wq, s, b):
+        """x (..., K) -> the gathered output (..., N) in this instance's buffer
+        for the shape (overwritten by the next call of the same shape)."""
+        k = x.shape[-1]
+        x2 = x.reshape(-1, k).contiguous()
+        out = self.out_buffer(x2.shape[0], wq.shape[0] * self.world, x.dtype)
         self.forward_into(x2, wq, s, b, out)
         return out.reshape(*x.shape[:-1], out.shape[-1])

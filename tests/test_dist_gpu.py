@@ -1,0 +1,97 @@
+"""Tensor-parallel qmm with the output gathered inside the kernel
+(tsb_qmm_w4g64_gather), on 2 GPUs: each rank's output holds every rank's
+columns, bit-identical to each shard's single-GPU result, across repeated
+calls into the same buffer, eager and replayed from a CUDA graph.
+
+Needs two GPUs (skipped otherwise): ranks that wait on one another never share
+a GPU."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import sys
+    from datetime import timedelta
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "mlx-tree-spec_b200"))
+    import torch.distributed as dist
+
+    import tsb
+    from tsb import dist as tdist
+    from tsb import ops
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        gq = tdist.GatheredQMM(world, rank)
+        errors = []
+        for (m, n, k) in [(16, 6144, 5120), (1, 1024, 1024), (64, 2048, 2560), (128, 1024, 640), (33, 3072, 1536)]:
+            g = torch.Generator(device="cuda").manual_seed(1000 + m + n)
+            wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda", generator=g) * 0.02)
+            x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+            shards = [tdist.shard_weight(wq, s, b, world, r) for r in range(world)]
+            ref = torch.cat([ops.quantized_matmul(x, *sh) for sh in shards], dim=1)
+            out = gq.out_buffer(m, n)
+            for rep in range(3):
+                out.fill_(0)
+                gq.forward_into(x, *shards[rank], out)
+                torch.cuda.synchronize()
+                if not torch.equal(out, ref):
+                    errors.append(f"eager {m}x{n}x{k} rep {rep}")
+            # captured: several calls into the same buffer per replay
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=side):
+                    for _ in range(4):
+                        gq.forward_into(x, *shards[rank], out)
+            torch.cuda.current_stream().wait_stream(side)
+            for rep in range(3):
+                graph.replay()
+                torch.cuda.synchronize()
+                if not torch.equal(out, ref):
+                    errors.append(f"graph {m}x{n}x{k} rep {rep}")
+            del graph
+        status = tsb._lib.load().tsb_device_status(None, 0)
+        torch.cuda.synchronize()
+        dist.barrier()
+        q.put((rank, errors, status))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, [repr(e)], -1))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_gathered_qmm_two_gpus():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errors, status in sorted(results):
+        assert not errors, (rank, errors)
+        assert status == 0, (rank, status)
