@@ -198,6 +198,43 @@ int tsb_tree_attn_noalloc(const void *q,
                           int B, int T, int Hq, int Hkv, int D, int n_kv, int tail, int kv_capacity,
                           float scale, void *out, float *lse, tsb_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Verify-step decoder layer: the kernels around the qmm and tree attention
+ * (mlx-tree-spec src/mlx_tree_spec/tree_verify.py:311-367 batch_attention /
+ * _attn_core, 414-447 batch_forward; fused_ops.py:107-154 add_rms_norm). All
+ * tensors bf16, row-major, 16-byte aligned; launches on `stream`.
+ * ---------------------------------------------------------------------- */
+
+/* Residual add + RMS norm (fused_ops.py:107-154): h = bf16(x + r),
+ * n = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) per row of D values. r NULL:
+ * the plain norm of x (nn.RMSNorm); h_out may be NULL. D % 8 == 0, D <= 8192. */
+int tsb_add_rms_norm(const void *x, const void *r, const void *w, void *h_out, void *n_out, int rows, int D,
+                     float eps, tsb_stream_t stream);
+
+/* Per-node q/k/v preparation for gated-q tree attention (tree_verify.py:
+ * 316-323, 331-362). qkv [B*T, ld]: per query head h the 2*D columns
+ * [h*2D, h*2D + D) query and [h*2D + D, (h+1)*2D) gate, then Hkv key heads,
+ * then Hkv value heads (D each). Queries and keys get the per-head RMS norm
+ * (q_norm / k_norm weights [D]) and mx.fast.rope (non-traditional, the first
+ * rope_dims dims, base, scale) at positions[b*T + t]; queries go to q_out
+ * [B, Hq, T, D]; keys and values are appended to the caches at rows
+ * offsets[b] + t (capacity rows per (request, head)) in kv_format, quantized on
+ * append for the 8-bit formats (TSB_KV_REF_Q8_ROW as kv8.py:39-43, MLX g64 as
+ * this library's quantizer). D == 256; rope_dims % 16 == 0. */
+int tsb_qkv_prep(const void *qkv, int ld, int B, int T, int Hq, int Hkv, int D, const void *q_norm,
+                 const void *k_norm, float eps, const int32_t *positions, int rope_dims, float rope_base,
+                 float rope_scale, void *q_out, int kv_format, void *k, void *k_scales, void *k_biases, void *v,
+                 void *v_scales, void *v_biases, int kv_capacity, const int32_t *offsets, tsb_stream_t stream);
+
+/* y [B*T, Hq*D] = attention out [B, Hq, T, D] * sigmoid(gate), the gate read
+ * from qkv as laid out above (tree_verify.py:327: o_proj's input). D == 256. */
+int tsb_attn_gate(const void *attn_out, const void *qkv, int ld, void *y, int B, int T, int Hq, int D,
+                  tsb_stream_t stream);
+
+/* SwiGLU: y [M, I] = silu(g) * u for gate_up [M, 2I] = [g | u] (the MLP's
+ * fused gate and up projections). I % 8 == 0. */
+int tsb_swiglu(const void *gate_up, void *y, int M, int I, tsb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,11 @@ SIGNATURES = {
     "tsb_tree_attn_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     "tsb_tree_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
                            _P, _P, _P, _Z, _P]),
+    "tsb_add_rms_norm": (_I, [_P, _P, _P, _P, _P, _I, _I, _F, _P]),
+    "tsb_qkv_prep": (_I, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _F, _P, _I, _F, _F, _P, _I, _P, _P, _P, _P, _P, _P,
+                          _I, _P, _P]),
+    "tsb_attn_gate": (_I, [_P, _P, _I, _P, _I, _I, _I, _I, _P]),
+    "tsb_swiglu": (_I, [_P, _P, _I, _I, _P]),
     "tsb_tree_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
                                    _P, _P, _P]),
 }

@@ -169,7 +169,7 @@ def _kv_planes(cache):
 
 
 def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None, stats: bool = False,
-               parents=None):
+               parents=None, out=None):
     """Tree-mask attention of `queries` (B, Hq, n, D) over `cache`.
 
     cache: any object with keys/values (B, Hkv, capacity, ...) and `offset`
@@ -183,7 +183,7 @@ def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None,
     Returns out (B, Hq, n, D) bf16, or (out, maxs, sums) with stats=True where
     maxs = log-sum-exp of each row's visible scores and sums = 1 (a single
     block: merge with more keys as tree_verify.py:389-401 does), or None when
-    declined."""
+    declined. `out` (optional): a (B, Hq, n, D) bf16 buffer to write into."""
     fmt, k, ks, kb, v, vs, vb = _kv_planes(cache)
     _require_cuda(queries, k, v)
     if queries.dtype != torch.bfloat16:
@@ -207,7 +207,7 @@ def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None,
         p = None
         tail_v = n if tail is None else int(tail)
     q = queries.contiguous()
-    out = torch.empty_like(q)
+    out = torch.empty_like(q) if out is None else out
     lse = torch.empty((bsz, hq, n), dtype=torch.float32, device=q.device) if stats else None
     lib = _lib.load()
     ws = workspace(lib.tsb_tree_attn_workspace_bytes(bsz, n, hq, hkv, d, n_kv, fmt), q.device)

@@ -264,3 +264,40 @@ def test_golden_attn_fixtures_regenerate():
         out = attention.tree_attention(bf16.bf16_bits_to_f32(g["q"]), kval, vval, int(g["n_kv"]), int(g["tail"]),
                                        g["bits"], float(g["scale"]))
         assert np.allclose(out, g["out"], atol=1e-5)
+
+
+def test_decoder_oracle_rope_and_norm():
+    """Self-checks of the decoder oracle (no GPU): rope is the identity at
+    position 0 and leaves dims >= rope_dims alone, turns pair (i, i + dims/2)
+    by pos * base^(-2i/dims); the RMS norm of a unit-weight row has unit RMS."""
+    import numpy as np
+
+    from oracle import decoder as od
+    from oracle.bf16 import round_bf16
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    r = od.rope(x, np.array([5, 0, 100]), 64, 1e7)
+    assert np.array_equal(r[1], round_bf16(x[1]))
+    assert np.array_equal(r[:, 64:], round_bf16(x[:, 64:]))
+    ang = 5 * 1e7 ** (-3 / 32)
+    assert abs(r[0, 3] - (x[0, 3] * np.cos(ang) - x[0, 35] * np.sin(ang))) < 1e-2
+    assert abs(r[0, 35] - (x[0, 3] * np.sin(ang) + x[0, 35] * np.cos(ang))) < 1e-2
+    _, n = od.rms_norm(x, np.ones(256), 1e-6)
+    assert np.allclose(np.sqrt(np.mean(n.astype(np.float64) ** 2, axis=-1)), 1, atol=1e-2)
+    h, _ = od.rms_norm(x, np.ones(256), 1e-6, r=x)
+    assert np.array_equal(h, round_bf16(2.0 * x.astype(np.float64)))
+
+
+def test_decoder_oracle_gate_and_swiglu():
+    import numpy as np
+
+    from oracle import decoder as od
+
+    gu = np.array([[0.0, 2.0, 3.0, -1.0]], dtype=np.float32)
+    a = od.swiglu(gu)
+    assert a[0, 0] == 0.0  # silu(0) = 0
+    assert abs(a[0, 1] - 2.0 / (1 + np.exp(-2.0)) * -1.0) < 2e-2
+    out = np.ones((1, 1, 1, 256), dtype=np.float32)
+    g = np.zeros((1, 1, 256), dtype=np.float32)
+    assert np.all(od.attn_gate(out, g) == 0.5)  # sigmoid(0) = 1/2
