@@ -466,6 +466,61 @@ def time_graph(fn, loops=10):
     return e0.elapsed_time(e1) * 1e3 / loops  # us per replay
 
 
+def build_decoder(fmt: str, layers: int = 16, seed: int = 1005):
+    """random-init 4-bit decoder, 4 requests x 32 tree nodes
+    over an 8K prefix per request (KV ~ N(0,1) in the given format)."""
+    import numpy as np
+    import torch
+
+    import tsb
+    from oracle import gen
+    from tsb import decoder as tdec
+
+    cfg = tdec.DecoderConfig(layers=layers)
+    weights, final_norm = tdec.random_weights(cfg, seed=seed)
+    b, t, prefix = 4, 32, 8192
+    cap = prefix + t
+    code = {"bf16": tsb.TSB_KV_BF16, "mlx_q8": tsb.TSB_KV_MLX_Q8_G64, "ref_q8": tsb.TSB_KV_REF_Q8_ROW}[fmt]
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    caches = []
+    for _ in range(cfg.layers):
+        kf = torch.randn(b, cfg.hkv, cap, cfg.d, device="cuda", generator=g)
+        vf = torch.randn(b, cfg.hkv, cap, cfg.d, device="cuda", generator=g)
+        caches.append(tdec.make_cache(kf, vf, prefix, code))
+        del kf, vf
+    rng = np.random.default_rng(seed)
+    parents = torch.from_numpy(np.stack([gen.tree_parents(rng, t) for _ in range(b)]).astype(np.int32)).cuda()
+    h0 = torch.randn(b * t, cfg.hidden, device="cuda", generator=g).to(torch.bfloat16)
+    return tdec.VerifyDecoder(cfg, weights, final_norm), h0, parents, caches, prefix
+
+
+def time_decoder_step(fmt: str):
+    """µs per verify step of config 5 (one CUDA graph per step)."""
+    import torch
+
+    dec, h0, parents, caches, prefix = build_decoder(fmt)
+    us = time_graph(lambda: dec.step(h0, parents, caches, prefix), loops=5)
+    n = dec.cfg.layers
+    del dec, caches
+    torch.cuda.empty_cache()
+    return us, n
+
+
+def run_profile_decoder(args):
+    """Config-5 decoder step (bf16 KV): --warmup steps, then one (for ncu)."""
+    import torch
+
+    import tsb
+
+    torch.cuda.set_device(0)
+    tsb.load_library()
+    dec, h0, parents, caches, prefix = build_decoder("bf16")
+    for _ in range(args.warmup + 1):
+        dec.step(h0, parents, caches, prefix)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "decoder", "steps": args.warmup + 1}))
+
+
 def run_secondary(pool, xs, hbm_peak, bf16_peak):
     """M=128 sweep, prefill M=4096, tree attention (config 4): reported beside
     the headline, not part of it."""
@@ -526,6 +581,17 @@ def run_secondary(pool, xs, hbm_peak, bf16_peak):
                                           "TFLOP/s": round(fl / us / 1e6, 1),
                                           "frac_hbm": round(byts / us / 1e3 / hbm_peak, 4)}
         del caches
+    # verify-step decoder, config 5: 16 layers over 4 requests x 32 nodes at 8K
+    for fmt in ("bf16", "mlx_q8"):
+        try:
+            us, layers = time_decoder_step(fmt)
+            out[f"decoder_step_config5_{fmt}"] = {
+                "us": round(us, 1), "layers": layers, "rows": 128, "context": 8192,
+                "note": "one CUDA graph per step: per layer 4 qmm (qkv 14336x5120, o 5120x6144, gate_up "
+                        "34816x5120, down 5120x17408 at M=128), qkv_prep, tree attention, gate, swiglu, "
+                        "2 add_rms_norm"}
+        except Exception as e:  # pragma: no cover - reported, not fatal
+            out[f"decoder_step_config5_{fmt}"] = {"error": str(e)[:200]}
     # unmasked attention comparator: torch SDPA on the same shape and the same 4 KV
     # heads (enable_gqa), bf16, no mask, K/V rotating through 4 caches like ours
     try:
@@ -621,7 +687,7 @@ def main():
     ap.add_argument("--impl", choices=["tsb", "reference"], default="tsb")
     ap.add_argument("--no-secondary", dest="secondary", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
-    ap.add_argument("--profile", choices=["qmm", "attn"], default=None,
+    ap.add_argument("--profile", choices=["qmm", "attn", "decoder"], default=None,
                     help="profiling driver for ncu: --warmup eager steps, then exactly one eager step "
                          "(qmm: the 15 sweep calls; attn: one config-4 B=1 L=32768 call); no timing")
     ap.add_argument("--attn-kv", choices=["bf16", "mlx_q8", "ref_q8"], default="bf16",
@@ -633,6 +699,8 @@ def main():
         run_reference(args)
     elif args.profile == "attn":
         run_profile_attn(args)
+    elif args.profile == "decoder":
+        run_profile_decoder(args)
     else:
         run_tsb(args)
 
