@@ -1,10 +1,10 @@
 """Tensor-parallel qmm with the output gathered inside the kernel
-(tsb_qmm_w4g64_gather), on 2 GPUs: each rank's output holds every rank's
-columns, bit-identical to each shard's single-GPU result, across repeated
-calls into the same buffer, eager and replayed from a CUDA graph.
+(tsb_qmm_w4g64_gather), on 2, 4 and 8 GPUs: each rank's output holds every
+rank's columns, bit-identical to each shard's single-GPU result, across
+repeated calls into the same buffer, eager and replayed from a CUDA graph.
 
-Needs two GPUs (skipped otherwise): ranks that wait on one another never share
-a GPU."""
+Each world size needs that many GPUs (skipped otherwise): ranks that wait on
+one another never share a GPU."""
 
 import os
 import socket
@@ -13,9 +13,6 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-
-WORLD = 2
-
 
 def _free_port():
     with socket.socket() as s:
@@ -79,14 +76,16 @@ def _worker(rank, world, port, q):
         q.put((rank, [repr(e)], -1))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
-def test_gathered_qmm_two_gpus():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gathered_qmm(world):
     import torch.multiprocessing as mp
 
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
