@@ -207,7 +207,7 @@ int tsb_tree_attn_noalloc(const void *q,
 
 /* Residual add + RMS norm (fused_ops.py:107-154): h = bf16(x + r),
  * n = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) per row of D values. r NULL:
- * the plain norm of x (nn.RMSNorm); h_out may be NULL. D % 8 == 0, D <= 8192. */
+ * the plain norm of x (nn.RMSNorm); h_out may be NULL. D % 8 == 0, D <= 16384. */
 int tsb_add_rms_norm(const void *x, const void *r, const void *w, void *h_out, void *n_out, int rows, int D,
                      float eps, tsb_stream_t stream);
 

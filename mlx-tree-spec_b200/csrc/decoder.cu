@@ -20,8 +20,8 @@
 namespace tsb {
 namespace {
 
-constexpr int NORM_THREADS = 256;
-constexpr int NORM_MAX_VEC = 4;  // 16-byte vectors per thread: D <= 8192
+constexpr int NORM_MAX_THREADS = 1024;
+constexpr int NORM_MAX_VEC = 2;  // 16-byte vectors per thread: D <= 16384
 
 TSB_HD float bf16r(float v) { return bf16_bits_to_float(float_to_bf16_bits(v)); }
 
@@ -40,16 +40,19 @@ TSB_HD uint4 pack8(const float (&f)[8]) {
 
 // h = bf16(x + r) (or x), n = bf16(w * bf16(h * rsqrt(mean(h^2) + eps))) per
 // row: fused_ops.py:107-129 (and mx.fast.rms_norm's rounding when r is null).
-__global__ void __launch_bounds__(NORM_THREADS)
+// One CTA per row, one thread per 16-byte vector (up to two): a row is one
+// round of loads, a block reduction and one round of stores.
+__global__ void __launch_bounds__(NORM_MAX_THREADS)
 add_rms_norm_kernel(const uint16_t *x, const uint16_t *r, const uint16_t *w, uint16_t *h_out, uint16_t *n_out, int D,
                     float eps) {
   const size_t base = (size_t)blockIdx.x * D;
   const int nv = D / 8;
+  const int nt = blockDim.x;
   float vals[NORM_MAX_VEC][8];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < NORM_MAX_VEC; ++i) {
-    const int c = threadIdx.x + i * NORM_THREADS;
+    const int c = threadIdx.x + i * nt;
     if (c < nv) {
       unpack8(*reinterpret_cast<const uint4 *>(x + base + 8 * c), vals[i]);
       if (r) {
@@ -63,18 +66,17 @@ add_rms_norm_kernel(const uint16_t *x, const uint16_t *r, const uint16_t *w, uin
       for (int e = 0; e < 8; ++e) ss = fmaf(vals[i][e], vals[i][e], ss);
     }
   }
-  __shared__ float red[NORM_THREADS / 32];
+  __shared__ float red[NORM_MAX_THREADS / 32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   float total = 0.f;
-#pragma unroll
-  for (int i = 0; i < NORM_THREADS / 32; ++i) total += red[i];
+  for (int i = 0; i < nt / 32; ++i) total += red[i];
   const float inv = rsqrtf(total / (float)D + eps);
 #pragma unroll
   for (int i = 0; i < NORM_MAX_VEC; ++i) {
-    const int c = threadIdx.x + i * NORM_THREADS;
+    const int c = threadIdx.x + i * nt;
     if (c < nv) {
       float wv[8], o[8];
       unpack8(*reinterpret_cast<const uint4 *>(w + 8 * c), wv);
@@ -118,8 +120,9 @@ TSB_HD void warp_rms_norm(float (&f)[8], const uint16_t *w, int lane, float eps)
 
 // mx.fast.rope, non-traditional, at one position: for i < dims/2 the pair
 // (x_i, x_{i+dims/2}) turns by pos * scale * base^(-2i/dims); dims..255 pass
-// through. Values of the pair partner come from lane +- dims/16.
-TSB_HD void warp_rope(float (&f)[8], int lane, int pos, int dims, float log2_base, float scale) {
+// through. Values of the pair partner come from lane +- dims/16; cos and sin
+// of the node's angles come from a table (cs, sn) the CTA builds once.
+TSB_HD void warp_rope(float (&f)[8], int lane, int dims, const float *cs_t, const float *sn_t) {
   const int half = dims / 2;
   const int dl = half / 8;  // lane distance of a pair
   const bool lo = lane < dl, hi = lane >= dl && lane < 2 * dl;
@@ -131,9 +134,7 @@ TSB_HD void warp_rope(float (&f)[8], int lane, int pos, int dims, float log2_bas
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int j = (lo ? lane : lane - dl) * 8 + e;  // frequency index in [0, half)
-    const float inv_freq = exp2f(-((float)j / (float)half) * log2_base);
-    float sn, cs;
-    sincosf((float)pos * scale * inv_freq, &sn, &cs);
+    const float cs = cs_t[j], sn = sn_t[j];
     f[e] = lo ? bf16r(f[e] * cs - p[e] * sn) : bf16r(p[e] * sn + f[e] * cs);
   }
 }
@@ -198,19 +199,27 @@ __global__ void __launch_bounds__(PREP_THREADS) qkv_prep_kernel(PrepArgs a) {
   const size_t cache_row0 = (size_t)a.offsets[b] + t;
   const uint16_t *row = a.qkv + (size_t)m * a.ld;
   const int nh = a.Hq + 2 * a.Hkv;
+  // the node's rope angles pos * scale * base^(-j/half), j < half, once
+  __shared__ float cs_t[128], sn_t[128];
+  const int half = a.rope_dims / 2;
+  for (int j = threadIdx.x; j < half; j += PREP_THREADS) {
+    const float inv_freq = exp2f(-((float)j / (float)half) * a.rope_log2_base);
+    sincosf((float)pos * a.rope_scale * inv_freq, &sn_t[j], &cs_t[j]);
+  }
+  __syncthreads();
   for (int hv = warp; hv < nh; hv += PREP_THREADS / 32) {
     float f[8];
     if (hv < a.Hq) {
       // query half of head hv (the gate half follows it)
       unpack8(*reinterpret_cast<const uint4 *>(row + (size_t)hv * 512 + 8 * lane), f);
       warp_rms_norm(f, a.q_norm, lane, a.eps);
-      warp_rope(f, lane, pos, a.rope_dims, a.rope_log2_base, a.rope_scale);
+      warp_rope(f, lane, a.rope_dims, cs_t, sn_t);
       *reinterpret_cast<uint4 *>(a.q_out + (((size_t)b * a.Hq + hv) * a.T + t) * 256 + 8 * lane) = pack8(f);
     } else if (hv < a.Hq + a.Hkv) {
       const int g = hv - a.Hq;
       unpack8(*reinterpret_cast<const uint4 *>(row + (size_t)a.Hq * 512 + (size_t)g * 256 + 8 * lane), f);
       warp_rms_norm(f, a.k_norm, lane, a.eps);
-      warp_rope(f, lane, pos, a.rope_dims, a.rope_log2_base, a.rope_scale);
+      warp_rope(f, lane, a.rope_dims, cs_t, sn_t);
       warp_append(a, a.k, a.ks, a.kb, ((size_t)b * a.Hkv + g) * a.cap + cache_row0, f, lane);
     } else {
       const int g = hv - a.Hq - a.Hkv;
@@ -264,11 +273,14 @@ extern "C" int tsb_add_rms_norm(const void *x, const void *r, const void *w, voi
                                 int D, float eps, tsb_stream_t stream) {
   if (!x || !w || !n_out) return TSB_EINVAL;
   if (rows <= 0 || D <= 0) return TSB_EINVAL;
-  if (D % 8 || D > NORM_THREADS * NORM_MAX_VEC * 8) return TSB_EUNSUPPORTED;
+  if (D % 8 || D > NORM_MAX_THREADS * NORM_MAX_VEC * 8) return TSB_EUNSUPPORTED;
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(n_out, 16) || (r && !aligned(r, 16)) ||
       (h_out && !aligned(h_out, 16)))
     return TSB_EINVAL;
-  add_rms_norm_kernel<<<rows, NORM_THREADS, 0, (cudaStream_t)stream>>>(
+  // one thread per 16-byte vector, in whole warps; beyond 1024 vectors, two each
+  const int nv = D / 8;
+  const int threads = nv <= NORM_MAX_THREADS ? (nv + 31) / 32 * 32 : NORM_MAX_THREADS;
+  add_rms_norm_kernel<<<rows, threads, 0, (cudaStream_t)stream>>>(
       (const uint16_t *)x, (const uint16_t *)r, (const uint16_t *)w, (uint16_t *)h_out, (uint16_t *)n_out, D, eps);
   return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
