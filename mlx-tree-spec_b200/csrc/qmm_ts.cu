@@ -93,7 +93,11 @@ struct TsCfg {
   static constexpr int TMEM_COLS = 512;
   static constexpr int CODES_WARP = 4, X_WARP = 5, DQ_WARP0 = 8;  // epilogue: warps 0-3
   static constexpr int THREADS = (NI > 2 ? 22 : 20) * 32;
-  static constexpr size_t SMEM = (size_t)STAGE_AREA + 1024 + 1024;
+  // epilogue: CW accumulator columns (tokens) per step; the step's bf16 outputs
+  // are staged in shared memory and leave as 16-byte chunks of y rows
+  static constexpr int CW = NI > 2 ? 8 : 16;
+  static constexpr int Y_STAGE = CW * ROWS * 2;
+  static constexpr size_t SMEM = (size_t)STAGE_AREA + 1024 + 1024 + Y_STAGE;
   static_assert(NC >= WGS && A_COL0 + WGS * SG * GA <= TMEM_COLS, "ring depths and TMEM columns");
   static_assert(CSLOT_BYTES % 1024 == 0 && XSLOT_BYTES % 1024 == 0, "slot alignment (128-byte swizzle atoms)");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
@@ -193,6 +197,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::STAGE_AREA);
+  uint16_t *ystage = reinterpret_cast<uint16_t *>(smem + C::STAGE_AREA + 1024);  // [CW][ROWS] bf16
   uint64_t *full_c = bars;                       // [NC] codes + scales + biases landed
   uint64_t *free_c = bars + C::NC;               // [NC] dequantizers have loaded the slot
   uint64_t *full_x = bars + 2 * C::NC;           // [NX] x landed
@@ -510,13 +515,13 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
           named_barrier_sync(1, 128);
         }
       }
-      const int row = tile * C::ROWS + r;
       // CW accumulator columns (tokens) at a time, every accumulator's chunk in
       // flight at once behind one wait (8 columns with 4 accumulators keeps it
-      // to 32 registers)
-      constexpr int CW = C::NI > 2 ? 8 : 16;
+      // to 32 registers); columns at or past M (padding tokens) are skipped by
+      // every part alike
+      constexpr int CW = C::CW;
 #pragma unroll 1
-      for (int c0 = 0; c0 < NP; c0 += CW) {
+      for (int c0 = 0; c0 < NP && c0 < a.M; c0 += CW) {
         uint32_t tv[C::NI][CW];
 #pragma unroll
         for (int uu = 0; uu < C::NI; ++uu)
@@ -571,12 +576,20 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
           named_barrier_sync(1, 128);
           peers_started = true;
         }
+        // bf16 outputs through shared memory: each thread holds one column of CW
+        // tokens; y rows go out in 16-byte chunks (eight columns of a token),
+        // to every rank's y
 #pragma unroll
-        for (int e = 0; e < CW; ++e)
-          if (c0 + e < a.M) {
-            const uint16_t h = float_to_bf16_bits(v[e]);
-            for (int pp = 0; pp < a.world; ++pp) a.yp[pp][(size_t)(c0 + e) * a.ldy + row] = h;
-          }
+        for (int e = 0; e < CW; ++e) ystage[e * C::ROWS + r] = float_to_bf16_bits(v[e]);
+        named_barrier_sync(1, 128);
+        const int ntok = min(CW, a.M - c0);
+        for (int i = threadIdx.x; i < ntok * (C::ROWS / 8); i += 128) {
+          const int e = i / (C::ROWS / 8), ch = i % (C::ROWS / 8);
+          const uint4 u = *reinterpret_cast<const uint4 *>(ystage + e * C::ROWS + ch * 8);
+          for (int pp = 0; pp < a.world; ++pp)
+            *reinterpret_cast<uint4 *>(a.yp[pp] + (size_t)(c0 + e) * a.ldy + (size_t)tile * C::ROWS + ch * 8) = u;
+        }
+        named_barrier_sync(1, 128);
       }
       // the accumulators are read: the issuers may start the next segment
       tc_fence_before();
