@@ -77,3 +77,57 @@ def test_workspace_sizes_are_host_computable(lib_built):
     assert lib.tsb_qmm_workspace_bytes(16, 6144, 5120) > 0
     assert lib.tsb_qmm_workspace_bytes(4096, 6144, 5120) == 0  # the prefill GEMM needs none
     assert lib.tsb_tree_attn_workspace_bytes(1, 32, 24, 4, 256, 32800, 0) > 0
+
+
+def test_gather_and_decoder_checks_before_any_launch(lib_built):
+    """The in-kernel-gather qmm and the decoder kernels refuse bad arguments on
+    the host (nothing is launched: the pointers below are never dereferenced)."""
+    import ctypes
+
+    from tsb import _lib
+
+    lib = _lib.load()
+    fake = 0x1000
+    g = _lib.GatherT()
+    g.world, g.rank = 2, 0
+    for p in range(2):
+        g.y[p], g.sig[p] = fake, fake
+
+    def gather(m=16, ns=1024, k=5120, ldy=2048, gg=g, x=fake):
+        return lib.tsb_qmm_w4g64_gather(x, fake, fake, fake, m, ns, k, ldy, ctypes.byref(gg) if gg else None,
+                                        fake, 1 << 20, None)
+
+    assert gather(x=None) == _lib.TSB_EINVAL
+    assert gather(gg=None) == _lib.TSB_EINVAL
+    assert gather(ns=1000) == _lib.TSB_EUNSUPPORTED  # shard rows not a multiple of 128
+    assert gather(m=129) == _lib.TSB_EUNSUPPORTED    # the verify path only
+    assert gather(ldy=1024) == _lib.TSB_EINVAL       # narrower than world * Ns
+    bad = _lib.GatherT()
+    bad.world, bad.rank = 2, 2
+    assert gather(gg=bad) == _lib.TSB_EINVAL         # rank out of range
+    bad.world, bad.rank = 9, 0
+    assert gather(gg=bad) == _lib.TSB_EINVAL         # more ranks than TSB_MAX_GATHER_RANKS
+    half = _lib.GatherT()
+    half.world, half.rank = 2, 1
+    half.y[0], half.sig[0] = fake, fake              # rank 1's buffers missing
+    assert gather(gg=half) == _lib.TSB_EINVAL
+
+    assert lib.tsb_add_rms_norm(fake, None, fake, None, fake, 4, 5121, 1e-6, None) == _lib.TSB_EUNSUPPORTED
+    assert lib.tsb_add_rms_norm(None, None, fake, None, fake, 4, 5120, 1e-6, None) == _lib.TSB_EINVAL
+    assert lib.tsb_add_rms_norm(fake, None, fake, None, fake, 4, 16392, 1e-6, None) == _lib.TSB_EUNSUPPORTED
+
+    def prep(**kw):
+        a = dict(ld=14336, B=4, T=32, Hq=24, Hkv=4, D=256, rope=64, base=1e7, fmt=0, cap=8224)
+        a.update(kw)
+        return lib.tsb_qkv_prep(fake, a["ld"], a["B"], a["T"], a["Hq"], a["Hkv"], a["D"], fake, fake, 1e-6, fake,
+                                a["rope"], a["base"], 1.0, fake, a["fmt"], fake, None, None, fake, None, None,
+                                a["cap"], fake, None)
+
+    assert prep(D=128) == _lib.TSB_EUNSUPPORTED
+    assert prep(rope=72) == _lib.TSB_EUNSUPPORTED   # rope dims must be a multiple of 16
+    assert prep(ld=14000) == _lib.TSB_EINVAL         # narrower than the q/gate/k/v columns
+    assert prep(fmt=1) == _lib.TSB_EINVAL            # MLX 8-bit without scales/biases
+    assert prep(fmt=5) == _lib.TSB_EUNSUPPORTED
+    assert prep(base=0.0) == _lib.TSB_EINVAL
+    assert lib.tsb_attn_gate(fake, fake, 1000, fake, 4, 32, 24, 256, None) == _lib.TSB_EINVAL
+    assert lib.tsb_swiglu(fake, fake, 128, 17404, None) == _lib.TSB_EUNSUPPORTED
