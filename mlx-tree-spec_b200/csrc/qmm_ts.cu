@@ -27,7 +27,9 @@
 //
 // Warp roles (thread = weight row = TMEM lane wherever TMEM is touched):
 //   warps 0-3  epilogue: per segment, accumulators -> registers -> y, partial
-//              or fixup; warp 0 also allocates TMEM.
+//              or fixup, 8 or 16 tokens at a time; y values are staged as bf16
+//              in shared memory and written as 16-byte chunks of y rows;
+//              warp 0 also allocates TMEM.
 //   warp 4     TMA producer of the codes ring: per stage the codes of the 128
 //              rows (32 words each, 128-byte swizzle) and their scales and
 //              biases (8-group boxes). A slot is refilled as soon as its
