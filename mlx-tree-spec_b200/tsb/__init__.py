@@ -4,7 +4,10 @@ Operators (reference-facing, over torch CUDA tensors):
   quantized_matmul, dequantize, ancestor_bits, tree_flash
 Containers: KVCache, Q8KVCache, MLXQ8KVCache
 Input makers: quantize, quantize_rows, quantize_g64
-Sharding: tsb.dist (N-sharded qmm with an NCCL all-gather)
+Sharding: tsb.dist (N-sharded qmm: GatheredQMM gathers the output inside the
+  kernel over NVLink; ShardedQMM uses an NCCL all-gather)
+Decoder: tsb.decoder (the verify-step layer stack of BASELINE config 5 over the
+  qmm, tree attention and the decoder-layer kernels)
 
 All compute runs in libtsb.so (sm_100a CUDA); importing the operators loads
 it and fails loudly if it is missing.
