@@ -235,6 +235,19 @@ int tsb_attn_gate(const void *attn_out, const void *qkv, int ld, void *y, int B,
  * fused gate and up projections). I % 8 == 0. */
 int tsb_swiglu(const void *gate_up, void *y, int M, int I, tsb_stream_t stream);
 
+/* Tree commit (tree_verify.py:487-496 _keep_kv; kv8.py:143-148 take_rows):
+ * for request b, rows offsets[b] + nodes[b*max_keep + i], i < n_keep[b], of
+ * every KV head's K and V (and their scales / biases in the 8-bit formats)
+ * move to rows offsets[b] + i. Rows are read before any is written, so a path
+ * may overlap its destination. offsets, nodes, n_keep are HOST arrays (copied
+ * into the launch's parameters; nothing is allocated or copied to the
+ * device). Caches laid out as for tsb_tree_attn. D == 256, B <= 8,
+ * max_keep <= 64, every node < 64 (the tree width bound); node and
+ * destination rows must lie below kv_capacity (else TSB_EINVAL). */
+int tsb_kv_commit(int kv_format, void *k, void *k_scales, void *k_biases, void *v, void *v_scales, void *v_biases,
+                  int B, int Hkv, int D, int kv_capacity, const int32_t *offsets, const int32_t *nodes,
+                  const int32_t *n_keep, int max_keep, tsb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,7 @@ from . import _lib
 from ._lib import (TSB_KV_BF16, TSB_KV_MLX_Q8_G64, TSB_KV_REF_Q8_ROW, TSBError,  # noqa: F401
                    load as load_library)
 from .cache import KVCache, MLXQ8KVCache, Q8KVCache  # noqa: F401
-from .ops import ancestor_bits, dequantize, quantized_matmul, tree_flash, workspace  # noqa: F401
+from .ops import ancestor_bits, commit, dequantize, keep_kv, quantized_matmul, tree_flash, workspace  # noqa: F401
 from .quant import quantize, quantize_g64, quantize_rows  # noqa: F401
 
 __version__ = "0.1.0"

@@ -56,6 +56,7 @@ SIGNATURES = {
     "tsb_swiglu": (_I, [_P, _P, _I, _I, _P]),
     "tsb_tree_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
                                    _P, _P, _P]),
+    "tsb_kv_commit": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _P]),
 }
 
 

@@ -14,6 +14,9 @@ same argument names and meaning:
   tree_flash(queries, cache, scale, bits, tail=None, stats=False)
       = tree_flash.tree_flash (tree_flash.py:151-196); also takes `parents=`
         so the mask is built inside the kernel.
+  keep_kv(cache, off0, nodes) / commit(caches, off0, nodes)
+      = tree_verify._keep_kv / the attention-cache part of tree_verify.commit
+        (tree_verify.py:487-516): keep the accepted path's K/V rows.
 
 Decline behaviour follows the reference: an unsupported shape or format
 returns None (the caller falls back), contract violations raise. All work is
@@ -22,6 +25,8 @@ workspace owned here (the C ABI itself never allocates).
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -219,3 +224,52 @@ def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None,
     if stats:
         return out, lse[..., None], torch.ones_like(lse)[..., None]
     return out
+
+
+def keep_kv(cache, off0, nodes):
+    """Keep only the accepted path of a finished tree pass in `cache`
+    (mlx-tree-spec src/mlx_tree_spec/tree_verify.py:487-496 _keep_kv; the int8
+    cache's take_rows, kv8.py:143-148): rows off0 + nodes[i] move to rows
+    off0 + i of every KV head's keys and values (and scales / biases).
+
+    off0 int with nodes a list of ints: the reference's form, the same path for
+    every request of the cache; cache.offset becomes off0 + len(nodes) and that
+    is returned. off0 a sequence with nodes a list of lists: one tree region
+    start and path per request; the new per-request offsets are returned (the
+    caller holds them) and cache.offset is left alone. A path equal to
+    range(len(path)) for every request moves nothing and launches nothing, as
+    the reference skips its take for a contiguous path."""
+    fmt, k, ks, kb, v, vs, vb = _kv_planes(cache)
+    _require_cuda(k, v)
+    if not all(t is None or t.is_contiguous() for t in (k, ks, kb, v, vs, vb)):
+        raise ValueError("keep_kv: cache tensors must be contiguous")
+    bsz, hkv, cap = k.shape[0], k.shape[1], k.shape[2]
+    per_request = not isinstance(off0, int)
+    offs = [int(o) for o in off0] if per_request else [int(off0)] * bsz
+    paths = [[int(i) for i in p] for p in nodes] if per_request else [[int(i) for i in nodes]] * bsz
+    if len(offs) != bsz or len(paths) != bsz:
+        raise ValueError(f"keep_kv: {len(offs)} offsets and {len(paths)} paths for {bsz} requests")
+    new_offs = [o + len(p) for o, p in zip(offs, paths)]
+    if any(p != list(range(len(p))) for p in paths):
+        d = (k.shape[3] * 4) if fmt == TSB_KV_MLX_Q8_G64 else k.shape[3]
+        max_keep = max(1, max(len(p) for p in paths))
+        flat = [0] * (bsz * max_keep)
+        for b, p in enumerate(paths):
+            flat[b * max_keep:b * max_keep + len(p)] = p
+        i32 = ctypes.c_int32
+        lib = _lib.load()
+        st = lib.tsb_kv_commit(fmt, _ptr(k), _ptr(ks), _ptr(kb), _ptr(v), _ptr(vs), _ptr(vb), bsz, hkv, d, cap,
+                               (i32 * bsz)(*offs), (i32 * len(flat))(*flat),
+                               (i32 * bsz)(*[len(p) for p in paths]), max_keep, _stream(k))
+        if check(st, "tsb_kv_commit") == TSB_EUNSUPPORTED:
+            raise ValueError(f"keep_kv: unsupported cache (D={d}, B={bsz}, path length {max_keep})")
+    if per_request:
+        return new_offs
+    cache.offset = new_offs[0]
+    return cache.offset
+
+
+def commit(caches, off0, nodes):
+    """keep_kv over every layer's cache (tree_verify.py:499-516 commit, its
+    attention-cache part: the KVCache layers and the MTP caches)."""
+    return [keep_kv(c, off0, nodes) for c in caches]

@@ -49,3 +49,14 @@ def dequant_g64(wq: np.ndarray, s_bits: np.ndarray, b_bits: np.ndarray, group_si
 
 
 __all__ = ["quantize_rows", "dequant_rows", "quantize_g64", "dequant_g64", "pack_bits"]
+
+
+def take_rows(t: np.ndarray, start: int, nodes) -> np.ndarray:
+    """A tree commit of one cache tensor [B, Hkv, cap, ...]
+    (tree_verify.py:487-496 _keep_kv, kv8.py:143-148 take_rows): rows
+    start + nodes move to start, start + 1, ... Returns the new tensor; the
+    gather reads the old rows before any is written, as mx.take does."""
+    out = np.array(t, copy=True)
+    idx = np.asarray(nodes, dtype=np.int64) + start
+    out[:, :, start:start + len(idx)] = np.take(np.asarray(t), idx, axis=2)
+    return out

@@ -131,3 +131,27 @@ def test_gather_and_decoder_checks_before_any_launch(lib_built):
     assert prep(base=0.0) == _lib.TSB_EINVAL
     assert lib.tsb_attn_gate(fake, fake, 1000, fake, 4, 32, 24, 256, None) == _lib.TSB_EINVAL
     assert lib.tsb_swiglu(fake, fake, 128, 17404, None) == _lib.TSB_EUNSUPPORTED
+
+    def keep(offs=(8, 8), paths=((0, 2, 3), (0, 1)), **kw):
+        a = dict(fmt=0, B=2, Hkv=4, D=256, cap=96, max_keep=3)
+        a.update(kw)
+        i32 = ctypes.c_int32
+        flat = [0] * (a["B"] * a["max_keep"])
+        for b, p in enumerate(paths[:a["B"]]):
+            flat[b * a["max_keep"]:b * a["max_keep"] + len(p)] = p
+        n = [len(p) for p in paths[:a["B"]]]
+        return lib.tsb_kv_commit(a["fmt"], fake, fake, fake, fake, fake, fake, a["B"], a["Hkv"], a["D"], a["cap"],
+                                 (i32 * a["B"])(*offs[:a["B"]]), (i32 * len(flat))(*flat), (i32 * a["B"])(*n),
+                                 a["max_keep"], None)
+
+    # host-side contract checks of the tree commit (no launch reaches the GPU)
+    assert keep(D=128) == _lib.TSB_EUNSUPPORTED
+    assert keep(B=9, offs=(0,) * 9, paths=((0,),) * 9) == _lib.TSB_EUNSUPPORTED  # more than 8 requests
+    assert keep(max_keep=65) == _lib.TSB_EUNSUPPORTED                             # path longer than 64
+    assert keep(fmt=3) == _lib.TSB_EUNSUPPORTED
+    assert keep(paths=((0, 2, 64), (0, 1))) == _lib.TSB_EINVAL                    # node past the tree width
+    assert keep(paths=((0, 2, -1), (0, 1))) == _lib.TSB_EINVAL
+    assert keep(offs=(8, 95)) == _lib.TSB_EINVAL                                  # destination past capacity
+    assert keep(paths=((0, 1, 2, 3), (0,)), max_keep=3) == _lib.TSB_EINVAL         # n_keep > max_keep
+    assert lib.tsb_kv_commit(0, None, None, None, fake, None, None, 1, 4, 256, 96, (ctypes.c_int32 * 1)(0),
+                             (ctypes.c_int32 * 1)(0), (ctypes.c_int32 * 1)(1), 1, None) == _lib.TSB_EINVAL

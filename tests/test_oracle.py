@@ -301,3 +301,19 @@ def test_decoder_oracle_gate_and_swiglu():
     out = np.ones((1, 1, 1, 256), dtype=np.float32)
     g = np.zeros((1, 1, 256), dtype=np.float32)
     assert np.all(od.attn_gate(out, g) == 0.5)  # sigmoid(0) = 1/2
+
+
+def test_take_rows_reads_before_writing():
+    """oracle.kv.take_rows against a row loop that reads every kept row first
+    (mx.take materialises the gather before the slice assignment,
+    tree_verify.py:491-494), on a path that overlaps its destination."""
+    from oracle import kv as okv
+
+    rng = np.random.default_rng(3)
+    t = rng.integers(-127, 128, size=(2, 3, 40, 16)).astype(np.int8)
+    for start, nodes in [(4, [0, 2, 3, 9]), (0, [1, 2, 3]), (7, []), (10, list(range(12)))]:
+        rows = [t[:, :, start + i].copy() for i in nodes]
+        want = t.copy()
+        for i, r in enumerate(rows):
+            want[:, :, start + i] = r
+        assert np.array_equal(okv.take_rows(t, start, nodes), want)
