@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tsb|reference]
 
-Headline workload (the verify-pass qmm sweep): one
+Headline workload (the verify-pass qmm sweep the headline metric is quoted on): one
 step = the 4-bit g64 quantized matmul at every M in {1, 8, 16, 32, 64} on each
 of the shapes (N, K) = (6144, 5120), (34816, 5120), (5120, 17408): 15 calls.
 metric = algorithmic bytes of those calls (codes + scales/biases + x + y) per
@@ -467,7 +467,7 @@ def time_graph(fn, loops=10):
 
 
 def build_decoder(fmt: str, layers: int = 16, seed: int = 1005):
-    """random-init 4-bit decoder, 4 requests x 32 tree nodes
+    """The decoder workload: random-init 4-bit decoder, 4 requests x 32 tree nodes
     over an 8K prefix per request (KV ~ N(0,1) in the given format)."""
     import numpy as np
     import torch

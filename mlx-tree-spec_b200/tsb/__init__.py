@@ -6,8 +6,11 @@ Containers: KVCache, Q8KVCache, MLXQ8KVCache
 Input makers: quantize, quantize_rows, quantize_g64
 Sharding: tsb.dist (N-sharded qmm: GatheredQMM gathers the output inside the
   kernel over NVLink; ShardedQMM uses an NCCL all-gather)
-Decoder: tsb.decoder (the verify-step layer stack of BASELINE config 5 over the
-  qmm, tree attention and the decoder-layer kernels)
+Decoder: tsb.decoder (the verify-step layer stack over the qmm, tree attention
+  and the decoder-layer kernels)
+Tree commit: keep_kv, commit (keep the accepted path's K/V rows)
+Checkpoints: tsb.checkpoint (mlx-lm safetensors -> device buffers, per-rank
+  row shards, fused q|k|v and gate|up)
 
 All compute runs in libtsb.so (sm_100a CUDA); importing the operators loads
 it and fails loudly if it is missing.

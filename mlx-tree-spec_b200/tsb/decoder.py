@@ -1,4 +1,4 @@
-"""The verify-step decoder on the library's kernels.
+"""The verify-step decoder (the gated-q layer stack) on the library's kernels.
 
 One step runs every layer of a gated-q decoder over the tree nodes of B
 requests (M = B*T rows), as mlx-tree-spec's batch_forward does

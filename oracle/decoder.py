@@ -1,4 +1,4 @@
-"""The verify-step decoder layer, restated on the CPU.
+"""The verify-step decoder layer (the gated-q layer), restated on the CPU.
 
 TEST INFRASTRUCTURE ONLY (see oracle/__init__.py).
 

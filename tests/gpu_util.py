@@ -30,7 +30,7 @@ def host_f32(t):
 
 
 def assert_close_rel(got, ref, rel=2e-2, what=""):
-    """max|got - ref| <= rel * max|ref| (the BASELINE tolerance for bf16 outputs)."""
+    """max|got - ref| <= rel * max|ref| (the tolerance for bf16 outputs)."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     assert got.shape == ref.shape, (got.shape, ref.shape)

@@ -1,7 +1,7 @@
 """GPU parity of tree masks and tree-mask attention against the oracle.
 
 Bar: ancestor masks bit-exact; attention max-abs-err <= 2e-2 * max|ref| for
-the bf16 output (BASELINE tolerance), and lse within 1e-2 absolute."""
+the bf16 output, and lse within 1e-2 absolute."""
 
 import glob
 import os
@@ -82,7 +82,8 @@ def test_attn_golden(path, mask_from):
 
 
 def _full_case(bsz, L, fmt, seed, t=32, hq=24, hkv=4, d=256, heads_checked=(0, 13, 23)):
-    """BASELINE config 4 at full size; the oracle checks a few query heads."""
+    """The attention benchmark shape (T=32, 24q/4kv heads, D=256) at full size; the
+    oracle checks a few query heads."""
     import tsb
 
     torch.manual_seed(seed)

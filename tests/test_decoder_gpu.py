@@ -4,7 +4,7 @@ oracle (oracle/decoder.py).
 Bars: the 8-bit appends are bit-exact against the oracle's quantizers applied
 to the kernel's own bf16 rows; the other outputs within 1e-2 * max|ref| per
 op (bf16 rounding of values computed with float32 rsqrt/exp/sincos), and the
-decoder step's output within the BASELINE 2e-2 * max|ref|."""
+decoder step's output within 2e-2 * max|ref|."""
 
 import numpy as np
 import pytest

@@ -47,7 +47,7 @@ def _worker(rank, world, port, ret):
 def test_sharded_qmm_gloo_world2():
     world = 2
     port = 29500 + (os.getpid() % 1000)
-    with mp.Manager() as man:
+    with mp.get_context("spawn").Manager() as man:
         ret = man.dict()
         mp.spawn(_worker, args=(world, port, ret), nprocs=world, join=True)
         assert ret.get(0) and ret.get(1)

@@ -1,7 +1,7 @@
 """GPU parity of the quantized matmul and dequantization against the oracle.
 
 Bar: dequantization bit-exact; qmm max-abs-err <= 2e-2 * max|ref| (bf16
-output, fp32 accumulation), the tolerance BASELINE.json states; the kernel is
+output, fp32 accumulation), the tolerance of the verify path; the kernel is
 also held to a much tighter bound against the exact result, since bf16
 rounding of the output alone is ~0.4%."""
 
@@ -18,7 +18,7 @@ from oracle import bf16, gen, qmm
 
 pytestmark = pytest.mark.gpu
 
-REL = 2e-2      # BASELINE tolerance
+REL = 2e-2      # the verify path's tolerance
 REL_TIGHT = 8e-3
 
 
@@ -50,7 +50,7 @@ def test_dequant_golden_bit_exact(path):
 
 
 def test_qmm_config1_seed0():
-    """x [16, 5120] ~ N(0,1), W [6144, 5120] ~ N(0, 0.02), seed 0."""
+    """The small case: x [16, 5120] ~ N(0,1), W [6144, 5120] ~ N(0, 0.02), seed 0."""
     x, wq, s, b = gen.config1()
     y = _run(x, wq, s, b)
     ref = qmm.qmm(x, wq, s, b)
@@ -61,7 +61,7 @@ def test_qmm_config1_seed0():
 @pytest.mark.parametrize("m", [1, 2, 5, 8, 16, 31, 32, 64, 65, 128])
 @pytest.mark.parametrize("nk", [(6144, 5120), (34816, 5120), (5120, 17408)])
 def test_qmm_sweep_sampled_rows(m, nk):
-    """BASELINE config 2 shapes at every sweep M (plus odd M); the oracle is
+    """The sweep shapes at every sweep M (plus odd M); the oracle is
     evaluated on a seeded sample of 384 output rows (all of K)."""
     import tsb
 
@@ -137,7 +137,7 @@ def test_qmm_gemm_path_full_oracle(m, n, k):
 
 @pytest.mark.parametrize("nk", [(34816, 5120), (5120, 17408), (6144, 5120)])
 def test_qmm_prefill_config3_sampled(nk):
-    """M = 4096; the oracle checks 48 x-rows x 256 weight rows."""
+    """The prefill case: M = 4096; the oracle checks 48 x-rows x 256 weight rows."""
     import tsb
 
     n, k = nk
