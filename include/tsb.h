@@ -248,6 +248,43 @@ int tsb_kv_commit(int kv_format, void *k, void *k_scales, void *k_biases, void *
                   int B, int Hkv, int D, int kv_capacity, const int32_t *offsets, const int32_t *nodes,
                   const int32_t *n_keep, int max_keep, tsb_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * GatedDeltaNet over tree nodes (the hybrid model's linear-attention layers;
+ * mlx-tree-spec tree_verify.py:149-238, fused_ops.py:28-104, 157-226). One
+ * request's n tree nodes per call. Dk = Dv = 128, Hv % Hk == 0 (else
+ * TSB_EUNSUPPORTED). bf16 tensors row-major, 8-byte aligned; state float32
+ * [Hv, Dv, Dk], 16-byte aligned. Node-major layouts: q, k [n, Hk, Dk];
+ * v, y [n, Hv, Dv]; g, beta, a, b [n, Hv]. C = (2*Hk + Hv) * 128.
+ * ---------------------------------------------------------------------- */
+
+/* gdn_prep (fused_ops.py:28-104): per node the causal conv (kernel 4) over
+ * rows conv_idx[node*4 + 0..3] of concat(conv_state [3, C], qkv [n, C]) with
+ * weights conv_w [C, 4], bf16, silu, bf16; v = that; q, k = per-head RMS norm
+ * (eps 1e-6, bf16) times 1/Dk and Dk^-1/2; beta = sigmoid(b) (bf16);
+ * g = exp(-exp(a_log) * bf16(softplus(bf16(a + dt_bias)))) (float32).
+ * a_log, dt_bias float32 [Hv]. conv_idx is a device array (n x 4). */
+int tsb_gdn_prep(const void *qkv, const void *conv_state, const int32_t *conv_idx, const void *conv_w, const void *a,
+                 const void *b, const float *a_log, const float *dt_bias, void *q, void *k, void *v, float *g,
+                 void *beta, int n, int Hk, int Dk, int Hv, int Dv, tsb_stream_t stream);
+
+/* tree_gated_delta (tree_verify.py:149-238): y[node] = the gated delta
+ * recurrence's output at `node` along its root path, from `state` (the
+ * committed state, not modified). Walks: device arrays paths, sibs
+ * [rows, lmax] (node indices, -1 past a walk's end / no sibling) and owner [n]
+ * (the walk that writes each node's output); every node must appear in some
+ * walk as a path node or a sibling. Out-of-range indices end a walk. */
+int tsb_tree_gated_delta(const void *q, const void *k, const void *v, const float *g, const void *beta,
+                         const float *state, const int32_t *paths, const int32_t *sibs, const int32_t *owner, int rows,
+                         int lmax, int n, int Hk, int Dk, int Hv, int Dv, void *y, tsb_stream_t stream);
+
+/* gdn_commit (fused_ops.py:157-226): state_out = the state after the accepted
+ * path nodes[0..n_keep) (a HOST int32 array, each < min(n, 64)) replayed from
+ * state_in (state_out may equal state_in); conv_out [3, C] = rows
+ * conv_idx[last*4 + 1..3] of concat(conv_state, qkv), last = nodes[n_keep-1]. */
+int tsb_gdn_commit(const void *k, const void *v, const float *g, const void *beta, const float *state_in,
+                   const void *conv_state, const void *qkv, const int32_t *conv_idx, const int32_t *nodes, int n_keep,
+                   int n, int Hk, int Dk, int Hv, int Dv, float *state_out, void *conv_out, tsb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,6 +11,8 @@ Decoder: tsb.decoder (the verify-step layer stack over the qmm, tree attention
 Tree commit: keep_kv, commit (keep the accepted path's K/V rows)
 Checkpoints: tsb.checkpoint (mlx-lm safetensors -> device buffers, per-rank
   row shards, fused q|k|v and gate|up)
+GatedDeltaNet: tsb.gdn (the hybrid model's linear-attention layers over tree
+  nodes: gdn_prep, tree_gated_delta, gdn_commit)
 
 All compute runs in libtsb.so (sm_100a CUDA); importing the operators loads
 it and fails loudly if it is missing.
