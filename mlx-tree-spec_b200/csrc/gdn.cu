@@ -10,10 +10,11 @@
 //           warp reduction.
 //   tree:   each node's recurrence output along its own root path. A walk is a
 //           root-to-leaf path; the host folds leaf siblings into walks as side
-//           steps from the same state (no extra state read). One warp per
-//           (walk, value head, dv row) holds that state row (Dk = 128 floats,
-//           4 per lane) in registers for the whole walk; 8 warps per CTA share
-//           the node's q/k through L1.
+//           steps from the same state (no extra state read). A CTA per (walk,
+//           value head, 32 dv rows) stages the walk's q/k/v/g/beta in shared
+//           memory in one parallel phase; each warp then runs the walk for 4
+//           state rows (4 x 128 floats in registers), its 4 dot products
+//           reduced together so the shuffles overlap.
 //   commit: the state after replaying the accepted path (nodes from the launch
 //           parameters), and the new conv state (the last node's window). Each
 //           lane reads its 4 state floats first and writes them last, so
@@ -131,61 +132,189 @@ struct TreeArgs {
   int n, rows, lmax, Hk, Hv;
 };
 
-// grid (Dv / 8, Hv, rows), 256 threads: warp w owns dv row blockIdx.x * 8 + w
+constexpr int kTreeRows = 4;                         // dv rows per warp
+constexpr int kTreeDv = kGdnWarps * kTreeRows;        // 32 dv rows per CTA
+constexpr int kStage = 32;                           // walk steps staged in shared memory
+
+// Butterfly sum of 4 independent values across the warp (interleaved for ILP).
+__device__ __forceinline__ void warp_sum4(float (&x)[kTreeRows]) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+#pragma unroll
+    for (int r = 0; r < kTreeRows; ++r) x[r] += __shfl_xor_sync(0xffffffffu, x[r], o);
+  }
+}
+
+__device__ __forceinline__ void unpack4(uint2 u, float (&f)[4]) {
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162 *>(&u.x);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162 *>(&u.y);
+  f[0] = __low2float(lo); f[1] = __high2float(lo); f[2] = __low2float(hi); f[3] = __high2float(hi);
+}
+
+// One walk step's inputs for this CTA: q/k of the node (and of its side leaf),
+// g and beta, and v of the CTA's 32 dv rows.
+struct StepIn {
+  uint2 q[32], k[32], qs[32], ks[32];   // lane l holds dk 4l..4l+3
+  __nv_bfloat16 v[kTreeDv], vs[kTreeDv];
+  float g, gs, beta, betas;
+  int node, sib;                        // -1: walk over / no side leaf
+  int own, owns;                        // this walk writes the node's / side leaf's output
+};
+
+// grid (Dv / 32, Hv, rows), 256 threads. Warp w owns dv rows
+// blockIdx.x * 32 + 4w .. +3 and keeps their state (4 x 4 floats per lane) in
+// registers for the whole walk. The first kStage steps' inputs are staged in
+// shared memory up front (all loads in flight at once); later steps load
+// directly.
 __global__ void __launch_bounds__(256) gdn_tree_kernel(TreeArgs a) {
+  __shared__ StepIn s_in[kStage];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int dv = blockIdx.x * kGdnWarps + warp;
+  const int dv_cta = blockIdx.x * kTreeDv;
+  const int dv0 = dv_cta + warp * kTreeRows;
   const int hv = blockIdx.y, row = blockIdx.z;
   const int hk = hv / (a.Hv / a.Hk);
-  float st[4];
-  {
-    const float4 s4 = *reinterpret_cast<const float4 *>(a.state + ((size_t)hv * kGdnD + dv) * kGdnD + lane * 4);
-    st[0] = s4.x; st[1] = s4.y; st[2] = s4.z; st[3] = s4.w;
+  const int staged = a.lmax < kStage ? a.lmax : kStage;
+
+  // stage 1: node / side-leaf indices and their scalars
+  for (int t = threadIdx.x; t < staged; t += blockDim.x) {
+    int node = a.paths[row * a.lmax + t];
+    int sib = a.sibs[row * a.lmax + t];
+    if (node < 0 || node >= a.n) node = -1;
+    if (sib < 0 || sib >= a.n || node < 0) sib = -1;
+    StepIn &si = s_in[t];
+    si.node = node;
+    si.sib = sib;
+    si.own = node >= 0 && a.owner[node] == row;
+    si.owns = sib >= 0 && a.owner[sib] == row;
+    if (node >= 0) {
+      si.g = a.g[node * a.Hv + hv];
+      si.beta = __bfloat162float(a.beta[node * a.Hv + hv]);
+    }
+    if (sib >= 0) {
+      si.gs = a.g[sib * a.Hv + hv];
+      si.betas = __bfloat162float(a.beta[sib * a.Hv + hv]);
+    }
+  }
+  __syncthreads();
+  // stage 2: vectors. Per step: 4 x 32 uint2 of q/k and 2 x 32 bf16 of v
+  for (int i = threadIdx.x; i < staged * 32; i += blockDim.x) {
+    const int t = i >> 5, l = i & 31;
+    StepIn &si = s_in[t];
+    if (si.node >= 0) {
+      const size_t qk = ((size_t)si.node * a.Hk + hk) * kGdnD + l * 4;
+      si.q[l] = *reinterpret_cast<const uint2 *>(a.q + qk);
+      si.k[l] = *reinterpret_cast<const uint2 *>(a.k + qk);
+      si.v[l] = a.v[((size_t)si.node * a.Hv + hv) * kGdnD + dv_cta + l];
+    }
+    if (si.sib >= 0) {
+      const size_t qk = ((size_t)si.sib * a.Hk + hk) * kGdnD + l * 4;
+      si.qs[l] = *reinterpret_cast<const uint2 *>(a.q + qk);
+      si.ks[l] = *reinterpret_cast<const uint2 *>(a.k + qk);
+      si.vs[l] = a.v[((size_t)si.sib * a.Hv + hv) * kGdnD + dv_cta + l];
+    }
+  }
+  __syncthreads();
+
+  float st[kTreeRows][4];
+#pragma unroll
+  for (int r = 0; r < kTreeRows; ++r) {
+    const float4 s4 = *reinterpret_cast<const float4 *>(a.state + ((size_t)hv * kGdnD + dv0 + r) * kGdnD + lane * 4);
+    st[r][0] = s4.x; st[r][1] = s4.y; st[r][2] = s4.z; st[r][3] = s4.w;
   }
   for (int t = 0; t < a.lmax; ++t) {
-    const int node = a.paths[row * a.lmax + t];
-    if (node < 0 || node >= a.n) break;
-    const int sib = a.sibs[row * a.lmax + t];
-    if (sib >= 0 && sib < a.n) {
+    int node, sib, own, owns;
+    float g, beta, gs = 0.f, betas = 0.f;
+    float qn[4], kn[4], qs[4], ks[4], vn[kTreeRows], vsv[kTreeRows];
+    if (t < kStage) {
+      const StepIn &si = s_in[t];
+      node = si.node;
+      if (node < 0) break;
+      sib = si.sib; own = si.own; owns = si.owns;
+      g = si.g; beta = si.beta;
+      unpack4(si.q[lane], qn);
+      unpack4(si.k[lane], kn);
+#pragma unroll
+      for (int r = 0; r < kTreeRows; ++r) vn[r] = __bfloat162float(si.v[warp * kTreeRows + r]);
+      if (sib >= 0) {
+        gs = si.gs; betas = si.betas;
+        unpack4(si.qs[lane], qs);
+        unpack4(si.ks[lane], ks);
+#pragma unroll
+        for (int r = 0; r < kTreeRows; ++r) vsv[r] = __bfloat162float(si.vs[warp * kTreeRows + r]);
+      }
+    } else {
+      node = a.paths[row * a.lmax + t];
+      if (node < 0 || node >= a.n) break;
+      sib = a.sibs[row * a.lmax + t];
+      if (sib >= a.n) sib = -1;
+      own = a.owner[node] == row;
+      owns = sib >= 0 && a.owner[sib] == row;
+      g = a.g[node * a.Hv + hv];
+      beta = __bfloat162float(a.beta[node * a.Hv + hv]);
+      load4(a.q + ((size_t)node * a.Hk + hk) * kGdnD + lane * 4, qn);
+      load4(a.k + ((size_t)node * a.Hk + hk) * kGdnD + lane * 4, kn);
+#pragma unroll
+      for (int r = 0; r < kTreeRows; ++r) vn[r] = __bfloat162float(a.v[((size_t)node * a.Hv + hv) * kGdnD + dv0 + r]);
+      if (sib >= 0) {
+        gs = a.g[sib * a.Hv + hv];
+        betas = __bfloat162float(a.beta[sib * a.Hv + hv]);
+        load4(a.q + ((size_t)sib * a.Hk + hk) * kGdnD + lane * 4, qs);
+        load4(a.k + ((size_t)sib * a.Hk + hk) * kGdnD + lane * 4, ks);
+#pragma unroll
+        for (int r = 0; r < kTreeRows; ++r)
+          vsv[r] = __bfloat162float(a.v[((size_t)sib * a.Hv + hv) * kGdnD + dv0 + r]);
+      }
+    }
+    if (sib >= 0) {
       // a leaf sibling: one step from the same state, not kept
-      float qs[4], ks[4];
-      load4(a.q + ((size_t)sib * a.Hk + hk) * kGdnD + lane * 4, qs);
-      load4(a.k + ((size_t)sib * a.Hk + hk) * kGdnD + lane * 4, ks);
-      const float gs = a.g[sib * a.Hv + hv];
-      float kv = 0.f;
+      float kv[kTreeRows], os[kTreeRows];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) kv += st[i] * gs * ks[i];
-      kv = warp_sum(kv);
-      const size_t vi = (size_t)sib * a.Hv + hv;
-      const float ds = (__bfloat162float(a.v[vi * kGdnD + dv]) - kv) * __bfloat162float(a.beta[vi]);
-      float os = 0.f;
+      for (int r = 0; r < kTreeRows; ++r) {
+        kv[r] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) os += (st[i] * gs + ks[i] * ds) * qs[i];
-      os = warp_sum(os);
-      if (lane == 0 && a.owner[sib] == row) a.y[vi * kGdnD + dv] = __float2bfloat16_rn(os);
+        for (int i = 0; i < 4; ++i) kv[r] += st[r][i] * gs * ks[i];
+      }
+      warp_sum4(kv);
+#pragma unroll
+      for (int r = 0; r < kTreeRows; ++r) {
+        const float ds = (vsv[r] - kv[r]) * betas;
+        os[r] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) os[r] += (st[r][i] * gs + ks[i] * ds) * qs[i];
+      }
+      warp_sum4(os);
+      if (lane == 0 && owns) {
+        const float o4[4] = {os[0], os[1], os[2], os[3]};
+        store4(a.y + ((size_t)sib * a.Hv + hv) * kGdnD + dv0, o4);
+      }
     }
-    float qn[4], kn[4];
-    load4(a.q + ((size_t)node * a.Hk + hk) * kGdnD + lane * 4, qn);
-    load4(a.k + ((size_t)node * a.Hk + hk) * kGdnD + lane * 4, kn);
-    const float gv = a.g[node * a.Hv + hv];
-    float kv = 0.f;
+    float kv[kTreeRows], out[kTreeRows];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      st[i] *= gv;
-      kv += st[i] * kn[i];
-    }
-    kv = warp_sum(kv);
-    const size_t vi = (size_t)node * a.Hv + hv;
-    const float delta = (__bfloat162float(a.v[vi * kGdnD + dv]) - kv) * __bfloat162float(a.beta[vi]);
-    float out = 0.f;
+    for (int r = 0; r < kTreeRows; ++r) {
+      kv[r] = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      st[i] += kn[i] * delta;
-      out += st[i] * qn[i];
+      for (int i = 0; i < 4; ++i) {
+        st[r][i] *= g;
+        kv[r] += st[r][i] * kn[i];
+      }
     }
-    out = warp_sum(out);
+    warp_sum4(kv);
+#pragma unroll
+    for (int r = 0; r < kTreeRows; ++r) {
+      const float delta = (vn[r] - kv[r]) * beta;
+      out[r] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        st[r][i] += kn[i] * delta;
+        out[r] += st[r][i] * qn[i];
+      }
+    }
+    warp_sum4(out);
     // shared nodes are walked by several rows; the first row that has one writes it
-    if (lane == 0 && a.owner[node] == row) a.y[vi * kGdnD + dv] = __float2bfloat16_rn(out);
+    if (lane == 0 && own) {
+      const float o4[4] = {out[0], out[1], out[2], out[3]};
+      store4(a.y + ((size_t)node * a.Hv + hv) * kGdnD + dv0, o4);
+    }
   }
 }
 
@@ -276,11 +405,11 @@ extern "C" int tsb_tree_gated_delta(const void *q, const void *k, const void *v,
   if (!q || !k || !v || !g || !beta || !state || !paths || !sibs || !owner || !y) return TSB_EINVAL;
   if (n <= 0 || rows <= 0 || lmax <= 0 || rows > 65535) return TSB_EINVAL;
   if (!gdn_heads_ok(Hk, Dk, Hv, Dv) || Hv > 65535) return TSB_EUNSUPPORTED;
-  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(state, 16)) return TSB_EINVAL;
+  if (!aligned(q, 8) || !aligned(k, 8) || !aligned(y, 8) || !aligned(state, 16)) return TSB_EINVAL;
   TreeArgs t{static_cast<const __nv_bfloat16 *>(q), static_cast<const __nv_bfloat16 *>(k),
              static_cast<const __nv_bfloat16 *>(v), static_cast<const __nv_bfloat16 *>(beta), g, state, paths, sibs,
              owner, static_cast<__nv_bfloat16 *>(y), n, rows, lmax, Hk, Hv};
-  gdn_tree_kernel<<<dim3(kGdnD / kGdnWarps, Hv, rows), 256, 0, (cudaStream_t)stream>>>(t);
+  gdn_tree_kernel<<<dim3(kGdnD / kTreeDv, Hv, rows), 256, 0, (cudaStream_t)stream>>>(t);
   return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 

@@ -42,12 +42,18 @@ def _inputs(seed, n, hk, hv):
                 dt_bias=torch.randn(hv, device="cuda", generator=g))
 
 
-@pytest.mark.parametrize("seed,n,hk,hv", [(0, 24, 2, 4), (1, 64, 16, 48), (2, 5, 1, 1)])
+def _deep(n):
+    """A 40-node chain with side leaves at depths 21, 35 and 36: walk steps past
+    the 32 the tree kernel stages in shared memory, side leaves on both sides."""
+    return list(range(-1, 39)) + [34, 35, 20][:n - 40]
+
+
+@pytest.mark.parametrize("seed,n,hk,hv", [(0, 24, 2, 4), (1, 64, 16, 48), (2, 5, 1, 1), (3, 43, 2, 4)])
 def test_prep_recurrence_commit(seed, n, hk, hv):
     from tsb import gdn
 
     rng = np.random.default_rng(seed)
-    parents = _tree(rng, n)
+    parents = _deep(n) if n == 43 else _tree(rng, n)
     x = _inputs(seed, n, hk, hv)
     q, k, v, g, beta = gdn.gdn_prep(x["qkv"], x["conv_state"], gdn.conv_idx(parents, "cuda"), x["conv_w"], x["a"],
                                     x["b"], x["A_log"], x["dt_bias"], hk, 128, hv, 128)
