@@ -1,7 +1,9 @@
 /*
  * tsb.h — C ABI of libtsb.so, the B200 (sm_100a) verify-pass hot path of
  * mlx-tree-spec: the MLX 4-bit affine quantized matmul and tree-mask flash
- * attention over a long KV prefix.
+ * attention over a long KV prefix, and the kernels either side of them (the
+ * decoder layer's norms, rope and KV append, the tree commit of the KV
+ * caches, GatedDeltaNet over tree nodes).
  *
  * Conventions (mirroring the reference's operator contract):
  *   - Every entry point returns an int status. TSB_OK on success.
@@ -247,6 +249,15 @@ int tsb_swiglu(const void *gate_up, void *y, int M, int I, tsb_stream_t stream);
 int tsb_kv_commit(int kv_format, void *k, void *k_scales, void *k_biases, void *v, void *v_scales, void *v_biases,
                   int B, int Hkv, int D, int kv_capacity, const int32_t *offsets, const int32_t *nodes,
                   const int32_t *n_keep, int max_keep, tsb_stream_t stream);
+
+/* The same commit for every layer's cache in one launch (tree_verify.py:
+ * 499-516 commit loops over the layers): k, v, k_scales ... are HOST arrays
+ * of `layers` device pointers (the scale / bias arrays NULL where the format
+ * has none), all caches of one format and shape. layers <= 48. */
+int tsb_kv_commit_layers(int kv_format, int layers, void *const *k, void *const *k_scales, void *const *k_biases,
+                         void *const *v, void *const *v_scales, void *const *v_biases, int B, int Hkv, int D,
+                         int kv_capacity, const int32_t *offsets, const int32_t *nodes, const int32_t *n_keep,
+                         int max_keep, tsb_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * GatedDeltaNet over tree nodes (the hybrid model's linear-attention layers;

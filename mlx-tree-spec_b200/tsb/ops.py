@@ -226,6 +226,44 @@ def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None,
     return out
 
 
+def _commit_plan(bsz: int, off0, nodes):
+    """(per_request, offsets, paths, new offsets) of a commit over bsz requests."""
+    per_request = not isinstance(off0, int)
+    offs = [int(o) for o in off0] if per_request else [int(off0)] * bsz
+    paths = [[int(i) for i in p] for p in nodes] if per_request else [[int(i) for i in nodes]] * bsz
+    if len(offs) != bsz or len(paths) != bsz:
+        raise ValueError(f"keep_kv: {len(offs)} offsets and {len(paths)} paths for {bsz} requests")
+    return per_request, offs, paths, [o + len(p) for o, p in zip(offs, paths)]
+
+
+def _commit_launch(caches, offs, paths):
+    """One tsb_kv_commit_layers launch over caches of one format and shape."""
+    planes = [_kv_planes(c) for c in caches]
+    fmt = planes[0][0]
+    k0 = planes[0][1]
+    for pl in planes:
+        _require_cuda(pl[1], pl[4])
+        if not all(t is None or t.is_contiguous() for t in pl[1:]):
+            raise ValueError("keep_kv: cache tensors must be contiguous")
+        if pl[0] != fmt or pl[1].shape != k0.shape or pl[1].dtype != k0.dtype or pl[1].device != k0.device:
+            raise ValueError("commit: every cache of one launch must share format, shape and device")
+    bsz, hkv, cap = k0.shape[0], k0.shape[1], k0.shape[2]
+    d = (k0.shape[3] * 4) if fmt == TSB_KV_MLX_Q8_G64 else k0.shape[3]
+    max_keep = max(1, max(len(p) for p in paths))
+    flat = [0] * (bsz * max_keep)
+    for b, p in enumerate(paths):
+        flat[b * max_keep:b * max_keep + len(p)] = p
+    i32, vp = ctypes.c_int32, ctypes.c_void_p
+    n = len(planes)
+    arrays = [(vp * n)(*[_ptr(pl[j]) for pl in planes]) if planes[0][j] is not None else None for j in range(1, 7)]
+    lib = _lib.load()
+    st = lib.tsb_kv_commit_layers(fmt, n, arrays[0], arrays[1], arrays[2], arrays[3], arrays[4], arrays[5], bsz, hkv,
+                                  d, cap, (i32 * bsz)(*offs), (i32 * len(flat))(*flat),
+                                  (i32 * bsz)(*[len(p) for p in paths]), max_keep, _stream(k0))
+    if check(st, "tsb_kv_commit_layers") == TSB_EUNSUPPORTED:
+        raise ValueError(f"keep_kv: unsupported cache (D={d}, B={bsz}, path length {max_keep}, {n} layers)")
+
+
 def keep_kv(cache, off0, nodes):
     """Keep only the accepted path of a finished tree pass in `cache`
     (mlx-tree-spec src/mlx_tree_spec/tree_verify.py:487-496 _keep_kv; the int8
@@ -239,37 +277,34 @@ def keep_kv(cache, off0, nodes):
     caller holds them) and cache.offset is left alone. A path equal to
     range(len(path)) for every request moves nothing and launches nothing, as
     the reference skips its take for a contiguous path."""
-    fmt, k, ks, kb, v, vs, vb = _kv_planes(cache)
-    _require_cuda(k, v)
-    if not all(t is None or t.is_contiguous() for t in (k, ks, kb, v, vs, vb)):
-        raise ValueError("keep_kv: cache tensors must be contiguous")
-    bsz, hkv, cap = k.shape[0], k.shape[1], k.shape[2]
-    per_request = not isinstance(off0, int)
-    offs = [int(o) for o in off0] if per_request else [int(off0)] * bsz
-    paths = [[int(i) for i in p] for p in nodes] if per_request else [[int(i) for i in nodes]] * bsz
-    if len(offs) != bsz or len(paths) != bsz:
-        raise ValueError(f"keep_kv: {len(offs)} offsets and {len(paths)} paths for {bsz} requests")
-    new_offs = [o + len(p) for o, p in zip(offs, paths)]
-    if any(p != list(range(len(p))) for p in paths):
-        d = (k.shape[3] * 4) if fmt == TSB_KV_MLX_Q8_G64 else k.shape[3]
-        max_keep = max(1, max(len(p) for p in paths))
-        flat = [0] * (bsz * max_keep)
-        for b, p in enumerate(paths):
-            flat[b * max_keep:b * max_keep + len(p)] = p
-        i32 = ctypes.c_int32
-        lib = _lib.load()
-        st = lib.tsb_kv_commit(fmt, _ptr(k), _ptr(ks), _ptr(kb), _ptr(v), _ptr(vs), _ptr(vb), bsz, hkv, d, cap,
-                               (i32 * bsz)(*offs), (i32 * len(flat))(*flat),
-                               (i32 * bsz)(*[len(p) for p in paths]), max_keep, _stream(k))
-        if check(st, "tsb_kv_commit") == TSB_EUNSUPPORTED:
-            raise ValueError(f"keep_kv: unsupported cache (D={d}, B={bsz}, path length {max_keep})")
-    if per_request:
-        return new_offs
-    cache.offset = new_offs[0]
-    return cache.offset
+    return commit([cache], off0, nodes)[0]
+
+
+_MAX_LAYERS_PER_LAUNCH = 48
 
 
 def commit(caches, off0, nodes):
     """keep_kv over every layer's cache (tree_verify.py:499-516 commit, its
-    attention-cache part: the KVCache layers and the MTP caches)."""
-    return [keep_kv(c, off0, nodes) for c in caches]
+    attention-cache part: the KVCache layers and the MTP caches), as one
+    launch per 48 caches of the same format and shape. Returns each cache's
+    keep_kv result."""
+    caches = list(caches)
+    if not caches:
+        return []
+    k0 = _kv_planes(caches[0])[1]
+    per_request, offs, paths, new_offs = _commit_plan(k0.shape[0], off0, nodes)
+    if any(p != list(range(len(p))) for p in paths):
+        groups: dict = {}
+        for c in caches:
+            fmt, k = _kv_planes(c)[:2]
+            groups.setdefault((fmt, tuple(k.shape), k.dtype, str(k.device)), []).append(c)
+        for group in groups.values():
+            if group[0] is not caches[0] and _kv_planes(group[0])[1].shape[0] != k0.shape[0]:
+                raise ValueError("commit: every cache must hold the same requests")
+            for i in range(0, len(group), _MAX_LAYERS_PER_LAUNCH):
+                _commit_launch(group[i:i + _MAX_LAYERS_PER_LAUNCH], offs, paths)
+    if per_request:
+        return [list(new_offs) for _ in caches]
+    for c in caches:
+        c.offset = new_offs[0]
+    return [new_offs[0]] * len(caches)

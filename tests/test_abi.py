@@ -155,3 +155,15 @@ def test_gather_and_decoder_checks_before_any_launch(lib_built):
     assert keep(paths=((0, 1, 2, 3), (0,)), max_keep=3) == _lib.TSB_EINVAL         # n_keep > max_keep
     assert lib.tsb_kv_commit(0, None, None, None, fake, None, None, 1, 4, 256, 96, (ctypes.c_int32 * 1)(0),
                              (ctypes.c_int32 * 1)(0), (ctypes.c_int32 * 1)(1), 1, None) == _lib.TSB_EINVAL
+
+    def layers(n, k=fake, v=fake):
+        vp, i32 = ctypes.c_void_p, ctypes.c_int32
+        ks = (vp * n)(*[k] * n)
+        vs = (vp * n)(*([v] * (n - 1) + [None]))   # the last layer's V pointer missing
+        return lib.tsb_kv_commit_layers(0, n, ks, None, None, vs, None, None, 1, 4, 256, 96, (i32 * 1)(0),
+                                        (i32 * 2)(0, 2), (i32 * 1)(2), 2, None)
+
+    assert layers(49) == _lib.TSB_EUNSUPPORTED      # more than 48 layers per launch
+    assert layers(3) == _lib.TSB_EINVAL             # a null plane in layer 2
+    assert lib.tsb_kv_commit_layers(0, 0, None, None, None, None, None, None, 1, 4, 256, 96, None, None, None, 1,
+                                    None) == _lib.TSB_EINVAL

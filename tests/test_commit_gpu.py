@@ -110,3 +110,23 @@ def test_keep_kv_empty_path_and_declines():
         tsb.keep_kv(c, [0, 0], [[0, 70], [0]])      # node past the 64-node tree width
     with pytest.raises(ValueError):
         tsb.keep_kv(c, [0, 0, 0], [[0], [0], [0]])  # three paths for two requests
+
+
+def test_commit_many_layers_one_launch():
+    """commit() over caches of two formats: one launch per format group, each
+    cache equal to the oracle's gather with its own data."""
+    import tsb
+
+    caches = [_cache(fmt, 3, 2, 80, seed=30 + i) for i, fmt in enumerate((1, 1, 0, 1, 0))]
+    before = [{n: _bytes(t) for n, t in _tensors(c).items()} for c in caches]
+    offs = [5, 11, 40]
+    paths = [[0, 3, 4, 9], [0, 1, 2, 3, 7], [0, 2]]
+    out = tsb.commit(caches, offs, paths)
+    torch.cuda.synchronize()
+    assert out == [[9, 16, 42]] * len(caches)
+    for c, b0 in zip(caches, before):
+        for name, t in _tensors(c).items():
+            want = b0[name].copy()
+            for i in range(3):
+                want[i:i + 1] = kv.take_rows(b0[name][i:i + 1], offs[i], paths[i])
+            assert np.array_equal(_bytes(t), want), name
