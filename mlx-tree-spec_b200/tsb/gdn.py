@@ -40,6 +40,9 @@ class Walks:
 
 
 def _check_parents(parents) -> tuple:
+    """parents: a sequence of parent indices, or a tree object carrying them in
+    `.parents` (as the reference's Tree does)."""
+    parents = getattr(parents, "parents", parents)
     p = tuple(int(x) for x in parents)
     if not p or p[0] != -1 or any(not 0 <= q < i for i, q in enumerate(p) if i):
         raise ValueError("parents: node 0 is the root (-1) and every other parent precedes its node")

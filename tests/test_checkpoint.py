@@ -122,3 +122,33 @@ def test_decoder_config(tmp_path):
     assert (c.layers, c.hidden, c.hq, c.hkv, c.d, c.inter, c.rope_dims, c.rope_base) == \
         (48, 5120, 24, 4, 256, 17408, 64, 1e7)
     assert os.path.exists(tmp_path / "model.safetensors.index.json")
+
+
+def test_decoder_layers_fuse_on_cpu(tmp_path):
+    """decoder_layers reads an mlx-lm layout (separate q/k/v and gate/up) back
+    into the decoder's fused projections, bit-exact, with the config's shapes."""
+    from ckpt_util import decoder_config_json, decoder_tensors
+    from tsb.checkpoint import Checkpoint, decoder_config, decoder_layers
+    from tsb.decoder import DecoderConfig
+
+    cfg = DecoderConfig(layers=2, hidden=256, hq=2, hkv=1, d=256, inter=256)
+    rng = np.random.default_rng(5)
+    norm = lambda n: torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(torch.bfloat16)  # noqa: E731
+    layers = [{"qkv": _w(rng, cfg.qkv_rows, cfg.hidden), "o": _w(rng, cfg.hidden, cfg.hq * cfg.d),
+               "gate_up": _w(rng, 2 * cfg.inter, cfg.hidden), "down": _w(rng, cfg.hidden, cfg.inter),
+               "q_norm": norm(cfg.d), "k_norm": norm(cfg.d), "input_norm": norm(cfg.hidden),
+               "post_norm": norm(cfg.hidden)} for _ in range(cfg.layers)]
+    final = norm(cfg.hidden)
+    write_checkpoint(str(tmp_path), decoder_tensors(cfg, layers, final), decoder_config_json(cfg))
+    ck = Checkpoint(str(tmp_path))
+    assert decoder_config(ck) == cfg
+    got, got_final = decoder_layers(ck, cfg, device="cpu")
+    for a, b in zip(layers, got):
+        for key in ("qkv", "o", "gate_up", "down"):
+            for x, y in zip(a[key], b[key]):
+                assert np.array_equal(_bits(x), _bits(y)), key
+        for key in ("q_norm", "k_norm", "input_norm", "post_norm"):
+            assert np.array_equal(_bits(a[key]), _bits(b[key])), key
+    assert np.array_equal(_bits(final), _bits(got_final))
+    with pytest.raises(ValueError):
+        decoder_layers(ck, DecoderConfig(layers=2, hidden=256, hq=4, hkv=1, d=256, inter=256), device="cpu")

@@ -91,3 +91,14 @@ def test_abi_host_checks():
     assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, nodes, 0, 8, 2, 128, 4, 128, f, f, None) == E.TSB_EINVAL
     long = (ctypes.c_int32 * 65)(*range(65))
     assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, long, 65, 80, 2, 128, 4, 128, f, f, None) == E.TSB_EUNSUPPORTED
+
+
+def test_walks_take_a_tree_object():
+    from tsb.gdn import walks
+
+    class Tree:
+        parents = (-1, 0, 0, 1)
+
+    a, b = walks(Tree()), walks([-1, 0, 0, 1])
+    assert (a.rows, a.sibs, a.owner, a.lmax) == (b.rows, b.sibs, b.owner, b.lmax)
+    assert np.array_equal(a.conv_idx, b.conv_idx)
