@@ -18,11 +18,13 @@
 // the stage's `empty` barrier before it refills the codes the dequantizers
 // wait on).
 //
-// Dequantization per packed word (8 codes): two masks and one shift split the
-// nibbles, three byte permutes place code | 0x4300 (= bf16 128 + q) in natural
-// order, an exact bf16 subtract of 128 gives q, and one bf16x2 fma rounds
-// s*q + b once to bf16 (the same value as bf16(fmaf(q, s, b)) whenever that
-// float32 sum is exact, i.e. for quantizer-produced weights).
+// Dequantization per packed word (8 codes): per pair of codes one byte permute
+// and one mask leave them as bf16 integers times 2^-133 / 2^-129, and one bf16x2
+// fma with (s * 2^133, s * 2^129) rounds s*q + b once to bf16 (dequant_word_sub;
+// scales of 2^-5 and above take the magic-number form, dequant_word, with the
+// same result). The reference rounds q*s + b to float32 first
+// (qmm_packed.py:635); the two agree unless that float32 rounding lands exactly
+// on a bf16 rounding midpoint, never for quantizer-produced weights.
 #include "sm100.cuh"
 
 namespace tsb {
@@ -171,10 +173,13 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         const int r = it * 32 + rsub;
         const uint32_t w = codes[r * 8 + j];
         const uint32_t sbv = sb_cur[it];
-        const __nv_bfloat162 s2 = u32_as_bf2((sbv & 0xFFFFu) | (sbv << 16));
         const __nv_bfloat162 b2 = u32_as_bf2((sbv >> 16) | (sbv & 0xFFFF0000u));
-        uint32_t o[4];
-        dequant_word(w, s2, b2, o);
+        uint32_t o[4], sp;
+        if (sub_scale_pair(sbv & 0xFFFFu, sp)) {
+          dequant_word_sub(w, u32_as_bf2(sp), b2, o);
+        } else {  // scales of 2^-5 and above, subnormal, inf or nan
+          dequant_word(w, u32_as_bf2((sbv & 0xFFFFu) | (sbv << 16)), b2, o);
+        }
         const uint32_t off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
         *reinterpret_cast<uint4 *>(btile + off) = make_uint4(o[0], o[1], o[2], o[3]);
       }

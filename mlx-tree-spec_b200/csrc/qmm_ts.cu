@@ -55,10 +55,14 @@
 // Every ring slot and every mbarrier has waiters that walk their stages (or
 // segments) in order, so no parity wait can run two phases ahead.
 //
-// Arithmetic: y = sum_k w_k x_k with w = bf16(fma(q, s, b)), the reference's
-// dequantization rule (qmm_packed.py:200, 348, 635) exactly: (code | 0x4300)
-// is bf16 128 + q, one bf16x2 subtract gives q exactly and one fused bf16x2
-// fma rounds q*s + b once. The weights carry the bias, so each group costs
+// Arithmetic: y = sum_k w_k x_k with w = bf16(q*s + b) rounded once (one bf16x2
+// fma per pair of codes after a byte permute and a mask: dequant_word_sub; the
+// magic-number form dequant_word for scales of 2^-5 and above). The reference
+// rounds q*s + b to float32 first (qmm_packed.py:200, 348, 635); the two agree
+// unless that float32 rounding lands exactly on a bf16 rounding midpoint, which
+// needs |b| below half a float32 ulp of q*s and never happens for
+// quantizer-made scales and biases. tsb_dequant_w4g64 follows the reference's
+// two roundings bit for bit. The weights carry the bias, so each group costs
 // only its four K=16 MMAs.
 #include "sm100.cuh"
 
@@ -426,13 +430,24 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         const uint32_t words[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         const uint32_t sb = (uint32_t)(s64 >> (16 * gl)) & 0xFFFFu;
         const uint32_t bb = (uint32_t)(b64 >> (16 * gl)) & 0xFFFFu;
-        const __nv_bfloat162 s2 = u32_as_bf2(sb | (sb << 16));
         const __nv_bfloat162 b2 = u32_as_bf2(bb | (bb << 16));
+        uint32_t sp;
+        if (sub_scale_pair(sb, sp)) {
 #pragma unroll
-        for (int wj = 0; wj < 8; ++wj) {
-          uint32_t o[4];
-          dequant_word(words[wj], s2, b2, o);
-          wt[4 * wj + 0] = o[0]; wt[4 * wj + 1] = o[1]; wt[4 * wj + 2] = o[2]; wt[4 * wj + 3] = o[3];
+          for (int wj = 0; wj < 8; ++wj) {
+            uint32_t o[4];
+            dequant_word_sub(words[wj], u32_as_bf2(sp), b2, o);
+            wt[4 * wj + 0] = o[0]; wt[4 * wj + 1] = o[1]; wt[4 * wj + 2] = o[2]; wt[4 * wj + 3] = o[3];
+          }
+        } else {
+          // scales of 2^-5 and above, subnormal, inf or nan: the exact slow form
+          const __nv_bfloat162 s2 = u32_as_bf2(sb | (sb << 16));
+#pragma unroll
+          for (int wj = 0; wj < 8; ++wj) {
+            uint32_t o[4];
+            dequant_word(words[wj], s2, b2, o);
+            wt[4 * wj + 0] = o[0]; wt[4 * wj + 1] = o[1]; wt[4 * wj + 2] = o[2]; wt[4 * wj + 3] = o[3];
+          }
         }
         tmem_st32(lane_base + C::A_COL0 + (wg * C::SG + gl) * C::GA, wt);
       }

@@ -209,3 +209,87 @@ def test_device_status_clean_after_runs():
 
     lib = _lib.load()
     assert lib.tsb_device_status(None, 0) == 0
+
+
+@pytest.mark.parametrize("m", [1, 3, 16, 33, 64, 100])
+@pytest.mark.parametrize("nk", [(256, 192), (384, 320), (128, 704), (640, 1088)])
+def test_qmm_verify_odd_group_counts(m, nk):
+    """K with a group count that is not a multiple of four (a partial last stage)
+    or of eight (scales and biases read directly, not by TMA)."""
+    n, k = nk
+    rng = np.random.default_rng(4200 + m + n + k)
+    x = gen.x_bf16(rng, m, k)
+    wq, s, b = gen.weights_w4g64(rng, n, k)
+    y = _run(x, wq, s, b)
+    ref = qmm.qmm(x, wq, s, b)
+    assert_close_rel(y, ref, REL_TIGHT, f"odd {m}x{n}x{k}")
+
+
+def _bf16_round_once(v):
+    """float64 -> bf16 value, one round-to-nearest-even from the exact value."""
+    mant, ex = np.frexp(v)
+    return np.ldexp(np.round(mant * 256) / 256, ex)
+
+
+@pytest.mark.parametrize("m", [1, 2, 4, 16, 32, 64, 128, 256])
+def test_effective_weights_rounding_rule(m):
+    """The weight each matmul path multiplies with, read back through one-hot x
+    rows (y[i] = W[:, k_i] exactly), for scale/bias pairs chosen so that q*s + b
+    is not exact in float32: large |b| against a small s, scales on both sides of
+    the kernels' 2^-5 fast-path limit, zero, subnormal and negative scales, and
+    crafted cases (q = 6, s = 129 * 2^a, b = -1.5 * 2^(a-17)) whose float32
+    rounding lands on a bf16 midpoint. The matmul kernels round q*s + b once
+    (bf16x2 fma); tsb_dequant_w4g64 rounds to float32 first, as the reference
+    does (qmm_packed.py:200, 348, 635). Both rules are pinned bit for bit, and
+    they differ only on the crafted midpoint cases."""
+    import tsb
+
+    rng = np.random.default_rng(5)
+    n, k = 256, 512
+    g_n = k // 64
+    codes = rng.integers(0, 16, size=(n, k)).astype(np.uint32)
+    s = np.zeros((n, g_n))
+    b = np.zeros((n, g_n))
+    crafted = np.zeros((n, g_n), dtype=bool)
+    for i in range(n):
+        for g in range(g_n):
+            f = i % 4
+            if f == 0:
+                s[i, g] = rng.uniform(0.002, 0.01)
+                b[i, g] = -rng.uniform(0.02, 0.08)
+            elif f == 1:
+                s[i, g] = rng.uniform(1e-6, 1e-4) * rng.choice([-1, 1])
+                b[i, g] = rng.uniform(1, 100) * rng.choice([-1, 1])
+            elif f == 2:
+                a = int(rng.integers(-20, -5))
+                s[i, g] = 129 * 2.0 ** a
+                b[i, g] = -1.5 * 2.0 ** (a - 17)
+                codes[i, g * 64:(g + 1) * 64:2] = 6
+                crafted[i, g] = True
+            else:
+                s[i, g] = [0.0, 1e-39, 0.5, -0.003, 3.0, -2e-5, 0.04, 2 ** -6][g % 8]
+                b[i, g] = rng.uniform(-1, 1)
+    s_bits = bf16.f32_to_bf16_bits(s.astype(np.float32))
+    b_bits = bf16.f32_to_bf16_bits(b.astype(np.float32))
+    sv = bf16.bf16_bits_to_f32(s_bits).astype(np.float64)
+    bv = bf16.bf16_bits_to_f32(b_bits).astype(np.float64)
+    exact = codes.reshape(n, g_n, 64) * sv[:, :, None] + bv[:, :, None]  # exact in float64
+    once = _bf16_round_once(exact).reshape(n, k)
+    twice = bf16.round_bf16(exact.astype(np.float32)).reshape(n, k).astype(np.float64)
+    differ = once != twice
+    assert differ.any() and np.all(np.repeat(crafted, 64, axis=1)[differ])
+    wq = np.zeros((n, k // 8), dtype=np.uint32)
+    for i in range(8):
+        wq |= codes[:, i::8] << (4 * i)
+    wd, sd, bd = dev_u32(wq), dev_bf16(s_bits), dev_bf16(b_bits)
+    deq = bf16.bf16_bits_to_f32(host_bf16_bits(tsb.dequantize(wd, sd, bd))).astype(np.float64)
+    assert np.array_equal(deq, twice)
+    got = np.zeros((n, k))
+    for k0 in range(0, k, m):
+        x = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
+        idx = torch.arange(m, device="cuda")
+        x[idx, (k0 + idx) % k] = 1
+        y = host_f32(tsb.quantized_matmul(x, wd, sd, bd))
+        for i in range(m):
+            got[:, (k0 + i) % k] = y[i]
+    assert np.array_equal(got, once), int(np.sum(got != once))
