@@ -41,12 +41,12 @@
 //              its share of every stage's groups into accumulator u (summed in
 //              the epilogue); per stage one wait, the MMAs back to back and two
 //              commits. A = the dequantized weights from TMEM, B = x from
-//              shared memory, f32 accumulators in TMEM. At N <= 64 an M=128
-//              K=16 MMA costs about the same whatever N is (~27 ns issued back
-//              to back), so independent accumulators from several issuers keep
-//              the tensor pipe busier than one dependent chain.
-//   warps 8-19 dequantizers, three warpgroups: warpgroup w owns the stages
-//              i = w (mod 3) of the CTA's range, all four groups of each:
+//              shared memory, f32 accumulators in TMEM. One thread issues at
+//              most one M=128 K=16 MMA every ~68 ns whatever N is, while four
+//              issuing warps reach ~17 ns per MMA at N <= 32 (measured on
+//              B200), so several issuers keep the tensor pipe busy.
+//   warps 8-19 dequantizers, three warpgroups (two at NP = 128): warpgroup w
+//              owns the stages i = w (mod WGS) of the CTA's range, all four groups:
 //              codes -> bf16(s*q + b) -> tcgen05.st into its own stage slot of
 //              A in TMEM, handed to the issuers once the stores have landed.
 //              Owning whole stages keeps the dequantizer warps of a
@@ -82,8 +82,11 @@ struct TsCfg {
   static constexpr int X_BOX_BYTES = NP * 128;     // one 64-K box of x
   static constexpr int XSLOT_BYTES = SG * X_BOX_BYTES;
   static constexpr int RING_BUDGET = 225 * 1024;   // shared memory for the two rings
-  static constexpr int WGS = 3;                    // dequantizer warpgroups = A stage slots
-  static constexpr int NI = NP <= 32 ? 4 : (NP <= 64 ? 2 : 1);  // MMA issuers, one accumulator each
+  // dequantizer warpgroups = A stage slots; at NP = 128 two, so that TMEM holds
+  // a second accumulator: one thread issues at most one M=128 K=16 MMA per
+  // ~68 ns whatever N is, so a single issuer would bound a stage at ~1.1 us
+  static constexpr int WGS = NP == 128 ? 2 : 3;
+  static constexpr int NI = NP <= 32 ? 4 : 2;      // MMA issuers, one accumulator each
   static constexpr int GPI = SG / NI;              // groups per issuer
   static constexpr int NX = NP <= 32 ? 4 : (NP == 64 ? 3 : 2);  // x slots
   static constexpr int NC_FIT = (RING_BUDGET - NX * XSLOT_BYTES) / CSLOT_BYTES;
@@ -235,10 +238,30 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     while (st >= a.nst) { st -= a.nst; ++tile; }
   };
 
+  auto cslot = [&](int s) { return smem + (size_t)s * C::CSLOT_BYTES; };
+  auto xslot = [&](int s) { return smem + C::X_AREA + (size_t)s * C::XSLOT_BYTES; };
+  // codes (and scales, biases) of local stage li into codes slot `slot`
+  auto issue_codes = [&](int li, int slot) {
+    int tile, st;
+    unit(li, tile, st);
+    const int gs = st * C::SG, n0 = tile * C::ROWS;
+    unsigned char *cs = cslot(slot);
+    mbar_arrive_expect_tx(&full_c[slot], C::C_BYTES + (sb_direct ? 0 : 2 * C::SB_BYTES));
+    tma_load_2d(cs, &tmap_w, gs * 8, n0, &full_c[slot]);
+    if (!sb_direct) {
+      const int gb = gs & ~7;  // 8-group box containing this stage's groups
+      tma_load_2d(cs + C::C_BYTES, &tmap_s, gb, n0, &full_c[slot]);
+      tma_load_2d(cs + C::C_BYTES + C::SB_BYTES, &tmap_b, gb, n0, &full_c[slot]);
+    }
+  };
+  const int first_loads = L < C::NC ? L : C::NC;
+
   if (threadIdx.x == 0) {
     // the next kernel on the stream may start its CTAs as this one's exit (it
     // waits for this grid before touching anything this grid writes)
     griddep_launch_dependents();
+  }
+  if (warp == C::CODES_WARP && lane == 0) {
     for (int s = 0; s < C::NC; ++s) {
       mbar_init(&full_c[s], 1);
       mbar_init(&free_c[s], 4);  // the 4 warps of the stage's warpgroup
@@ -257,6 +280,14 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     }
     fence_mbar_init();
     fence_proxy_async_smem();
+    // the weights, scales and biases are constant: the first ring's worth of
+    // them streams while TMEM is allocated and the other roles start
+    tma_prefetch_desc(&tmap_w);
+    if (!sb_direct) {
+      tma_prefetch_desc(&tmap_s);
+      tma_prefetch_desc(&tmap_b);
+    }
+    for (int li = 0; li < first_loads; ++li) issue_codes(li, li);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -266,58 +297,51 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  auto cslot = [&](int s) { return smem + (size_t)s * C::CSLOT_BYTES; };
-  auto xslot = [&](int s) { return smem + C::X_AREA + (size_t)s * C::XSLOT_BYTES; };
 
-  if (warp == C::CODES_WARP || warp == C::X_WARP) {
-    // ---------------- TMA producers
-    const bool codes = warp == C::CODES_WARP;
-    const int nslots = codes ? C::NC : C::NX;
-    uint64_t *full = codes ? full_c : full_x;
-    uint64_t *freed = codes ? free_c : free_x;
-    if (elect_one()) {
-      if (codes) {
-        tma_prefetch_desc(&tmap_w);
-        if (!sb_direct) {
-          tma_prefetch_desc(&tmap_s);
-          tma_prefetch_desc(&tmap_b);
-        }
-      } else {
-        tma_prefetch_desc(&tmap_x);
+  if (warp == C::CODES_WARP) {
+    // ---------------- TMA producer of the codes ring (its first NC stages were
+    // issued before the CTA-wide barrier)
+    if (lane == 0) {
+      Ring ring;
+      ring.slot = first_loads % C::NC;
+      ring.phase = first_loads == C::NC ? 1u : 0u;
+      int issued = first_loads;
+      for (int li = first_loads; li < L; ++li, ring.next(C::NC)) {
+        if (!mbar_wait(&free_c[ring.slot], ring.phase ^ 1u)) break;
+        issue_codes(li, ring.slot);
+        issued = li + 1;
       }
+      // drain: every issued load has landed before the CTA can exit
+      for (int i = (issued > C::NC ? issued - C::NC : 0); i < issued; ++i) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_c[i % C::NC], (i / C::NC) & 1)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
+        }
+      }
+    }
+  } else if (warp == C::X_WARP) {
+    // ---------------- TMA producer of the x ring; x may be the previous
+    // kernel's output
+    if (elect_one()) {
+      tma_prefetch_desc(&tmap_x);
       Ring ring;
       int issued = 0;
       int tile, st;
       unit(0, tile, st);
-      // x may be the previous kernel's output; the weights, scales and biases
-      // are constant, so their stream starts before that kernel has finished
-      if (!codes) griddep_wait();
-      for (int li = 0; li < L; ++li, ring.next(nslots), step(tile, st, 1)) {
-        if (li >= nslots && !mbar_wait(&freed[ring.slot], ring.phase ^ 1u)) break;
+      griddep_wait();
+      for (int li = 0; li < L; ++li, ring.next(C::NX), step(tile, st, 1)) {
+        if (li >= C::NX && !mbar_wait(&free_x[ring.slot], ring.phase ^ 1u)) break;
         const int gs = st * C::SG;
-        if (codes) {
-          unsigned char *cs = cslot(ring.slot);
-          const int n0 = tile * C::ROWS;
-          mbar_arrive_expect_tx(&full[ring.slot], C::C_BYTES + (sb_direct ? 0 : 2 * C::SB_BYTES));
-          tma_load_2d(cs, &tmap_w, gs * 8, n0, &full[ring.slot]);
-          if (!sb_direct) {
-            const int gb = gs & ~7;  // 8-group box containing this stage's groups
-            tma_load_2d(cs + C::C_BYTES, &tmap_s, gb, n0, &full[ring.slot]);
-            tma_load_2d(cs + C::C_BYTES + C::SB_BYTES, &tmap_b, gb, n0, &full[ring.slot]);
-          }
-        } else {
-          unsigned char *xt = xslot(ring.slot);
-          mbar_arrive_expect_tx(&full[ring.slot], C::XSLOT_BYTES);
+        unsigned char *xt = xslot(ring.slot);
+        mbar_arrive_expect_tx(&full_x[ring.slot], C::XSLOT_BYTES);
 #pragma unroll
-          for (int gl = 0; gl < C::SG; ++gl)
-            tma_load_2d(xt + gl * C::X_BOX_BYTES, &tmap_x, (gs + gl) * 64, 0, &full[ring.slot]);
-        }
+        for (int gl = 0; gl < C::SG; ++gl)
+          tma_load_2d(xt + gl * C::X_BOX_BYTES, &tmap_x, (gs + gl) * 64, 0, &full_x[ring.slot]);
         issued = li + 1;
       }
-      // drain: every issued load has landed before the CTA can exit
-      for (int i = (issued > nslots ? issued - nslots : 0); i < issued; ++i) {
+      for (int i = (issued > C::NX ? issued - C::NX : 0); i < issued; ++i) {
         const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[i % nslots], (i / nslots) & 1)) {
+        while (!mbar_try_wait(&full_x[i % C::NX], (i / C::NX) & 1)) {
           if (globaltimer_ns() - t0 > kWaitLimitNs) { record_status(TSB_ETIMEOUT); break; }
         }
       }
