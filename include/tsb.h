@@ -291,7 +291,9 @@ int tsb_tree_gated_delta(const void *q, const void *k, const void *v, const floa
 /* gdn_commit (fused_ops.py:157-226): state_out = the state after the accepted
  * path nodes[0..n_keep) (a HOST int32 array, each < min(n, 64)) replayed from
  * state_in (state_out may equal state_in); conv_out [3, C] = rows
- * conv_idx[last*4 + 1..3] of concat(conv_state, qkv), last = nodes[n_keep-1]. */
+ * conv_idx[last*4 + 1..3] of concat(conv_state, qkv), last = nodes[n_keep-1].
+ * conv_out must not overlap conv_state (TSB_EINVAL): other CTAs may still be
+ * reading conv_state while it is written. */
 int tsb_gdn_commit(const void *k, const void *v, const float *g, const void *beta, const float *state_in,
                    const void *conv_state, const void *qkv, const int32_t *conv_idx, const int32_t *nodes, int n_keep,
                    int n, int Hk, int Dk, int Hv, int Dv, float *state_out, void *conv_out, tsb_stream_t stream);

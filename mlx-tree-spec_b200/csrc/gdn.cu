@@ -385,6 +385,7 @@ extern "C" int tsb_gdn_prep(const void *qkv, const void *conv_state, const int32
     return TSB_EINVAL;
   if (n <= 0) return TSB_EINVAL;
   if (!gdn_heads_ok(Hk, Dk, Hv, Dv)) return TSB_EUNSUPPORTED;
+  if (n > 65535) return TSB_EUNSUPPORTED;  // one grid row per node
   if (!aligned(qkv, 8) || !aligned(conv_state, 8) || !aligned(conv_w, 8) || !aligned(q, 8) || !aligned(k, 8) ||
       !aligned(v, 8))
     return TSB_EINVAL;
@@ -423,6 +424,13 @@ extern "C" int tsb_gdn_commit(const void *k, const void *v, const float *g, cons
   if (!gdn_heads_ok(Hk, Dk, Hv, Dv) || Hv + 1 > 65535) return TSB_EUNSUPPORTED;
   if (n_keep > kGdnMaxPath) return TSB_EUNSUPPORTED;
   if (!aligned(k, 8) || !aligned(state_in, 16) || !aligned(state_out, 16)) return TSB_EINVAL;
+  {
+    // conv_out is written by several CTAs while others still read conv_state:
+    // the two [3, C] bf16 ranges must not overlap
+    const size_t bytes = (size_t)3 * (2 * Hk + Hv) * kGdnD * 2;
+    const uintptr_t s0 = reinterpret_cast<uintptr_t>(conv_state), o0 = reinterpret_cast<uintptr_t>(conv_out);
+    if (s0 < o0 + bytes && o0 < s0 + bytes) return TSB_EINVAL;
+  }
   CommitArgs c{};
   c.k = static_cast<const __nv_bfloat16 *>(k);
   c.v = static_cast<const __nv_bfloat16 *>(v);

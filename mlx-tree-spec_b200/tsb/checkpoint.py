@@ -341,31 +341,66 @@ LAYER_NAMES = {
 }
 
 
+def _rope_field(c: dict, key: str):
+    """A rope setting at the top level of the text config, or nested under
+    "rope_parameters" (the newer Hugging Face / mlx-lm layout); None if absent."""
+    if key in c:
+        return c[key]
+    return (c.get("rope_parameters") or {}).get(key)
+
+
 def decoder_config(ckpt: Checkpoint, **overrides):
     """A tsb.decoder.DecoderConfig from the checkpoint's config.json (its
-    "text_config" when nested). rope_dims = head_dim * partial_rotary_factor."""
+    "text_config" when nested). rope_theta and partial_rotary_factor are read
+    at the top level or under "rope_parameters"; a config with no rope_theta in
+    either place is refused (ValueError) rather than given a default base, and a
+    missing partial_rotary_factor means full rotary (1.0), its Hugging Face
+    meaning. rope_dims = head_dim * partial_rotary_factor."""
     from .decoder import DecoderConfig
 
     c = ckpt.config.get("text_config", ckpt.config)
     d = c.get("head_dim", c["hidden_size"] // c["num_attention_heads"])
+    theta = overrides.get("rope_base", _rope_field(c, "rope_theta"))
+    if theta is None:
+        raise ValueError("config has no rope_theta (top level or rope_parameters); pass rope_base=")
+    factor = _rope_field(c, "partial_rotary_factor")
     kw = dict(layers=c["num_hidden_layers"], hidden=c["hidden_size"], hq=c["num_attention_heads"],
               hkv=c.get("num_key_value_heads", c["num_attention_heads"]), d=d, inter=c["intermediate_size"],
-              eps=c.get("rms_norm_eps", 1e-6), rope_dims=int(d * c.get("partial_rotary_factor", 1.0)),
-              rope_base=c.get("rope_theta", 10000.0))
+              eps=c.get("rms_norm_eps", 1e-6), rope_dims=int(d * (1.0 if factor is None else factor)),
+              rope_base=float(theta))
     kw.update(overrides)
     return DecoderConfig(**kw)
 
 
-def decoder_layers(ckpt: Checkpoint, cfg, indices=None, prefix: str = "model.layers", final_norm: str = "model.norm",
+# Where mlx-lm checkpoints keep the text model's layers: plain decoders under
+# "model.layers", multimodal wrappers (e.g. qwen3_5) under the language model.
+LAYER_PREFIXES = ("model.layers", "language_model.model.layers", "model.language_model.layers")
+
+
+def decoder_layers(ckpt: Checkpoint, cfg, indices=None, prefix: str | None = None, final_norm: str | None = None,
                    device="cuda", names: dict | None = None):
     """(layers, final_norm) for tsb.decoder.VerifyDecoder, read from `ckpt`:
     q|k|v fused into one qkv projection, gate|up into gate_up, the norms as
     bf16. indices: the layer numbers to load (default: every layer with a
-    q_proj, i.e. the full-attention layers of a hybrid model)."""
+    q_proj, i.e. the full-attention layers of a hybrid model). prefix: where the
+    layers live (default: the first of LAYER_PREFIXES that holds a q_proj);
+    final_norm: the final norm's module (default: the prefix's ".norm")."""
     nm = dict(LAYER_NAMES, **(names or {}))
+
+    def layer_numbers(pfx):
+        return sorted(int(n.split(".")[len(pfx.split("."))]) for n in ckpt.tensors
+                      if n.startswith(pfx + ".") and n.endswith(nm["q"] + ".weight"))
+
+    if prefix is None:
+        prefix = next((p for p in LAYER_PREFIXES if layer_numbers(p)), None)
+        if prefix is None:
+            raise ValueError(f"no layer with a {nm['q']} under any of {LAYER_PREFIXES}; pass prefix=")
+    if final_norm is None:
+        final_norm = prefix[: -len(".layers")] + ".norm" if prefix.endswith(".layers") else "model.norm"
     if indices is None:
-        indices = sorted(int(n.split(".")[len(prefix.split("."))]) for n in ckpt.tensors
-                         if n.startswith(prefix + ".") and n.endswith(nm["q"] + ".weight"))
+        indices = layer_numbers(prefix)
+        if not indices:
+            raise ValueError(f"no layer with a {nm['q']} under {prefix!r}")
     layers = []
     for i in indices:
         p = f"{prefix}.{i}."

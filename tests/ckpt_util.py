@@ -57,7 +57,7 @@ def decoder_tensors(cfg, layers, final_norm, prefix: str = "model.layers") -> di
         for key, name in (("q_norm", "self_attn.q_norm"), ("k_norm", "self_attn.k_norm"),
                           ("input_norm", "input_layernorm"), ("post_norm", "post_attention_layernorm")):
             out[f"{p}{name}.weight"] = lw[key]
-    out["model.norm.weight"] = final_norm
+    out[prefix[: -len(".layers")] + ".norm.weight"] = final_norm
     return out
 
 

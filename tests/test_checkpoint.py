@@ -124,6 +124,31 @@ def test_decoder_config(tmp_path):
     assert os.path.exists(tmp_path / "model.safetensors.index.json")
 
 
+@pytest.mark.parametrize("where", ["top", "nested", "missing"])
+def test_decoder_config_rope_layouts(tmp_path, where):
+    """rope_theta / partial_rotary_factor at the top level or nested under
+    "rope_parameters" (newer configs); a config without rope_theta is refused
+    rather than given a default base."""
+    from tsb.checkpoint import Checkpoint, decoder_config
+
+    c = {"num_hidden_layers": 4, "hidden_size": 5120, "num_attention_heads": 24, "num_key_value_heads": 4,
+         "head_dim": 256, "intermediate_size": 17408, "rms_norm_eps": 1e-6}
+    rope = {"partial_rotary_factor": 0.25, "rope_theta": 1e7}
+    if where == "top":
+        c.update(rope)
+    elif where == "nested":
+        c["rope_parameters"] = dict(rope, rope_type="default")
+    write_checkpoint(str(tmp_path), {"a": torch.zeros(1)}, {"text_config": c}, n_files=1)
+    ck = Checkpoint(str(tmp_path))
+    if where == "missing":
+        with pytest.raises(ValueError):
+            decoder_config(ck)
+        assert decoder_config(ck, rope_base=5e6).rope_base == 5e6
+        return
+    cfg = decoder_config(ck)
+    assert (cfg.rope_dims, cfg.rope_base) == (64, 1e7)
+
+
 def test_decoder_layers_fuse_on_cpu(tmp_path):
     """decoder_layers reads an mlx-lm layout (separate q/k/v and gate/up) back
     into the decoder's fused projections, bit-exact, with the config's shapes."""
@@ -152,3 +177,28 @@ def test_decoder_layers_fuse_on_cpu(tmp_path):
     assert np.array_equal(_bits(final), _bits(got_final))
     with pytest.raises(ValueError):
         decoder_layers(ck, DecoderConfig(layers=2, hidden=256, hq=4, hkv=1, d=256, inter=256), device="cpu")
+
+
+def test_decoder_layers_find_the_language_model_prefix(tmp_path):
+    """Multimodal mlx-lm checkpoints keep the text layers under
+    language_model.model.layers (and the final norm beside them): found without
+    naming the prefix; a checkpoint with no q_proj anywhere is refused."""
+    from ckpt_util import decoder_config_json, decoder_tensors
+    from tsb.checkpoint import Checkpoint, decoder_layers
+    from tsb.decoder import DecoderConfig
+
+    cfg = DecoderConfig(layers=1, hidden=256, hq=2, hkv=1, d=256, inter=256)
+    rng = np.random.default_rng(6)
+    norm = lambda n: torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(torch.bfloat16)  # noqa: E731
+    layers = [{"qkv": _w(rng, cfg.qkv_rows, cfg.hidden), "o": _w(rng, cfg.hidden, cfg.hq * cfg.d),
+               "gate_up": _w(rng, 2 * cfg.inter, cfg.hidden), "down": _w(rng, cfg.hidden, cfg.inter),
+               "q_norm": norm(cfg.d), "k_norm": norm(cfg.d), "input_norm": norm(cfg.hidden),
+               "post_norm": norm(cfg.hidden)}]
+    final = norm(cfg.hidden)
+    write_checkpoint(str(tmp_path / "mm"), decoder_tensors(cfg, layers, final, prefix="language_model.model.layers"),
+                     decoder_config_json(cfg))
+    got, got_final = decoder_layers(Checkpoint(str(tmp_path / "mm")), cfg, device="cpu")
+    assert len(got) == 1 and np.array_equal(_bits(final), _bits(got_final))
+    write_checkpoint(str(tmp_path / "none"), {"model.norm.weight": final}, decoder_config_json(cfg), n_files=1)
+    with pytest.raises(ValueError):
+        decoder_layers(Checkpoint(str(tmp_path / "none")), cfg, device="cpu")

@@ -86,11 +86,18 @@ def test_abi_host_checks():
     assert lib.tsb_tree_gated_delta(f, f, f, f, f, f, f, f, f, 0, 4, 8, 2, 128, 4, 128, f, None) == E.TSB_EINVAL
     assert lib.tsb_tree_gated_delta(f, f, f, f, f, f + 8, f, f, f, 2, 4, 8, 2, 128, 4, 128, f, None) == E.TSB_EINVAL
     assert lib.tsb_tree_gated_delta(f, f, f, f, f, f, f, f, f, 2, 4, 8, 2, 128, 4, 96, f, None) == E.TSB_EUNSUPPORTED
+    # prep: more nodes than one grid dimension holds
+    assert lib.tsb_gdn_prep(f, f, f, f, f, f, f, f, f, f, f, f, f, 65536, 2, 128, 4, 128, None) == E.TSB_EUNSUPPORTED
     # commit: a path node outside the tree, an empty path, a path longer than 64
-    assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, nodes, 2, 1, 2, 128, 4, 128, f, f, None) == E.TSB_EINVAL
-    assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, nodes, 0, 8, 2, 128, 4, 128, f, f, None) == E.TSB_EINVAL
+    o = 0x1000000  # conv_out apart from conv_state
+    assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, nodes, 2, 1, 2, 128, 4, 128, f, o, None) == E.TSB_EINVAL
+    assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, nodes, 0, 8, 2, 128, 4, 128, f, o, None) == E.TSB_EINVAL
     long = (ctypes.c_int32 * 65)(*range(65))
-    assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, long, 65, 80, 2, 128, 4, 128, f, f, None) == E.TSB_EUNSUPPORTED
+    assert lib.tsb_gdn_commit(f, f, f, f, f, f, f, f, long, 65, 80, 2, 128, 4, 128, f, o, None) == E.TSB_EUNSUPPORTED
+    # commit: conv_out overlapping conv_state ([3, (2*2 + 4) * 128] bf16 = 6144 bytes)
+    cs = 0x100000
+    for out in (cs, cs + 6142, cs - 6142):
+        assert lib.tsb_gdn_commit(f, f, f, f, f, cs, f, f, nodes, 2, 8, 2, 128, 4, 128, f, out, None) == E.TSB_EINVAL
 
 
 def test_walks_take_a_tree_object():
