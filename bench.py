@@ -384,6 +384,8 @@ def run_tsb(args):
     launches_per_step = len(calls)  # one qmm kernel per call
 
     secondary = {}
+    if args.secondary and world > 1:
+        secondary = run_dist_secondary(world, rank, pool, xs, total_bytes, bf16_peak)
     if args.secondary and rank == 0 and world == 1:
         secondary = run_secondary(pool, xs, hbm_peak, bf16_peak)
 
@@ -574,12 +576,23 @@ def run_secondary(pool, xs, hbm_peak, bf16_peak):
                 tsb.tree_flash(q, c, d**-0.5, parents=parents)
 
         us = time_graph(f) / len(caches)
+        # the same kernel with the mask disabled (no tree rows: every key visible),
+        # the unmasked comparator of the 1.3x target
+        zero_bits = torch.zeros(t, dtype=torch.int64, device="cuda")
+
+        def fu():
+            for c in caches:
+                tsb.tree_flash(q, c, d**-0.5, bits=zero_bits, tail=0)
+
+        us_u = time_graph(fu) / len(caches)
         row = {"bf16": 512, "mlx_q8": 272, "ref_q8": 260}[fmt]
         byts = bsz * n_kv * hkv * row * 2 + 2 * bsz * t * hq * d * 2
         fl = 4.0 * bsz * t * hq * n_kv * d
         out[f"attn_B{bsz}_L{L}_{fmt}"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1),
                                           "TFLOP/s": round(fl / us / 1e6, 1),
-                                          "frac_hbm": round(byts / us / 1e3 / hbm_peak, 4)}
+                                          "frac_hbm": round(byts / us / 1e3 / hbm_peak, 4),
+                                          "us_unmasked": round(us_u, 2),
+                                          "masked_over_unmasked": round(us / us_u, 3)}
         del caches
     # verify-step decoder, config 5: 16 layers over 4 requests x 32 nodes at 8K
     for fmt in ("bf16", "mlx_q8"):
@@ -604,10 +617,101 @@ def run_secondary(pool, xs, hbm_peak, bf16_peak):
         byts = bsz * (L + t) * hkv * 512 * 2 + 2 * bsz * t * hq * d * 2
         out["sdpa_gqa_unmasked_B1_L32768_bf16"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1),
                                                    "note": "torch scaled_dot_product_attention, enable_gqa, no mask"}
+        try:
+            from flash_attn import flash_attn_func
+
+            qf = q.transpose(1, 2).contiguous()
+            kvf = [(k_.transpose(1, 2).contiguous(), v_.transpose(1, 2).contiguous()) for (k_, v_) in kv]
+            us_fa = time_graph(lambda: [flash_attn_func(qf, k_, v_) for (k_, v_) in kvf]) / len(kvf)
+            out["flash_attn_unmasked_B1_L32768_bf16"] = {"us": round(us_fa, 2), "GB/s": round(byts / us_fa / 1e3, 1),
+                                                         "note": "flash_attn.flash_attn_func (library), GQA, no mask"}
+            del kvf
+        except Exception as e:  # pragma: no cover - library comparator only
+            out["flash_attn_unmasked_B1_L32768_bf16"] = {"error": str(e)[:160]}
         del kv
     except Exception as e:  # pragma: no cover - comparator only
         out["sdpa_gqa_unmasked"] = {"error": str(e)[:160]}
     return out
+
+
+def run_dist_secondary(world, rank, pool, xs, total_bytes, bf16_peak):
+    """At N > 1, on every rank (the same collectives in the same order): the
+    sweep in the NCCL form (each rank's shard, then an all-gather and a re-layout
+    into the full output) beside the in-kernel gather of the headline, and
+    config 3 (prefill, M = 4096) N-sharded with the all-gather of each block of
+    rows overlapped against the next block's matmul."""
+    import torch
+
+    import tsb
+    from tsb import dist as tdist
+    from tsb import ops
+
+    out = {}
+    sq = tdist.ShardedQMM(world, rank)
+    calls = [(m, n, k) for m in SWEEP_M for (n, k) in SHAPES]
+    ys = {(m, n): torch.empty(m, n, dtype=torch.bfloat16, device="cuda") for (m, n, k) in calls}
+
+    def step():
+        used = {}
+        for (m, n, k) in calls:
+            c = used.get((n, k), 0)
+            used[(n, k)] = c + 1
+            wq, s, b = pool.shards[(n, k)][c % len(pool.shards[(n, k)])]
+            sq.forward_into(xs[(m, k)], wq, s, b, ys[(m, n)])
+
+    def timed(fn, reps):
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) * 1e3 / reps, world)  # us
+
+    for _ in range(3):
+        step()
+    us = timed(step, 10)
+    out["sweep_nccl_allgather"] = {"TB/s": round(total_bytes / us / 1e6, 4), "us_per_step": round(us, 1),
+                                   "note": "same 15 calls: shard matmul + NCCL all_gather + re-layout, eager"}
+    m = 4096
+    for (n, k) in ((34816, 5120), (5120, 17408)):
+        ns = n // world
+        g = torch.Generator(device="cuda").manual_seed(4000 + n + rank)
+        wq, s, b = tsb.quantize(torch.randn(ns, k, device="cuda", generator=g) * 0.02)
+        gx = torch.Generator(device="cuda").manual_seed(4100 + n)
+        x = torch.randn(m, k, device="cuda", generator=gx).to(torch.bfloat16)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        local = torch.empty(m, ns, dtype=torch.bfloat16, device="cuda")
+        res = {}
+        for chunks in (1, 4):
+            def f(chunks=chunks):
+                sq.forward_into(x, wq, s, b, y, chunks=chunks)
+            f()
+            res[chunks] = timed(f, 3)
+        ops.quantized_matmul_into(x, wq, s, b, local, ns)
+        us_local = timed(lambda: ops.quantized_matmul_into(x, wq, s, b, local, ns), 3)
+        best = min(res.values())
+        tf = 2.0 * m * n * k / best / 1e6
+        out[f"prefill_M4096_{n}x{k}_N{world}"] = {
+            "us": round(best, 1), "TFLOP/s": round(tf, 1), "frac_of_bf16_peak_per_gpu": round(tf / world / bf16_peak, 4),
+            "us_one_block": round(res[1], 1), "us_four_blocks_overlapped": round(res[4], 1),
+            "us_shard_matmul_alone": round(us_local, 1),
+            "note": "N-sharded, full [M, N] output on every rank (NCCL all_gather + re-layout)"}
+        del wq, s, b, x, y, local
+    return out
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def cpu_baseline_sample():
@@ -629,8 +733,8 @@ def cpu_baseline_sample():
         qmm.qmm_cpu(x, wq, s, b, threads)
         tot_t += time.perf_counter() - t0
         tot_b += alg_bytes(16, n, k)
-    return {"value": round(tot_b / tot_t / 1e12, 6), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": "oracle port (dequantize + f32 matmul), one M=16 call on each of the 3 shapes"}
+    return {"value": round(tot_b / tot_t / 1e12, 6), "unit": UNIT, "cores": threads, "cpu_model": cpu_model(),
+            "kind": "port", "sample": "oracle port (dequantize + f32 matmul), one M=16 call on each of the 3 shapes"}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -672,8 +776,8 @@ def run_reference(args):
         "config": {"workload": "verify-pass qmm sweep (bounded sample: one M=16 call per step, shapes cycled)",
                    "note": "reference kernels are Metal (MLX/MTPLX), unavailable on this box; "
                            "CPU port of its arithmetic"},
-        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "one M=16 qmm per step over the 3 shapes (dequantize + f32 matmul)"},
+        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "cpu_model": cpu_model(),
+                         "kind": "port", "sample": "one M=16 qmm per step over the 3 shapes (dequantize + f32 matmul)"},
         "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

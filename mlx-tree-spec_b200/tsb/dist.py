@@ -52,6 +52,7 @@ class ShardedQMM:
     def __init__(self, world: int, rank: int, group=None, local_op=None):
         self.world, self.rank, self.group = world, rank, group
         self._bufs: dict = {}
+        self._streams: dict = {}
         # local_op(x2, wq, s, b, y, ldy): the shard's matmul (the CUDA kernel by
         # default; tests substitute a CPU stand-in to check the host logic).
         if local_op is None:
@@ -69,16 +70,52 @@ class ShardedQMM:
             self._bufs[key] = b
         return b
 
-    def forward_into(self, x, wq, s, b, out):
-        """x (M, K) contiguous; (wq, s, b) this rank's shard; out (M, N) full."""
+    def _comm_stream(self, device):
+        st = self._streams.get(str(device))
+        if st is None:
+            st = torch.cuda.Stream(device=device)
+            self._streams[str(device)] = st
+        return st
+
+    def forward_into(self, x, wq, s, b, out, chunks: int = 1):
+        """x (M, K) contiguous; (wq, s, b) this rank's shard; out (M, N) full.
+
+        chunks > 1 (M a multiple of it): the shard's matmul runs `chunks` row
+        blocks of x in turn, and each block's all-gather and re-layout into
+        `out` run on a side stream while the next block computes (on CUDA; on
+        the CPU the blocks run in order), so the collective overlaps compute."""
         import torch.distributed as dist
 
         m = x.shape[0]
         ns = wq.shape[0]
         local, gathered = self._buf(m, ns, out.dtype, out.device)
-        self.local_op(x, wq, s, b, local, ns)
-        dist.all_gather_into_tensor(gathered.view(self.world * m, ns), local, group=self.group)
-        return gather_relayout(gathered, out)
+        if chunks <= 1 or m % chunks:
+            self.local_op(x, wq, s, b, local, ns)
+            dist.all_gather_into_tensor(gathered.view(self.world * m, ns), local, group=self.group)
+            return gather_relayout(gathered, out)
+        c = m // chunks
+        blocks = gathered.view(chunks, self.world, c, ns)  # one contiguous [world, c, ns] per block
+        if not x.is_cuda:
+            for i in range(chunks):
+                self.local_op(x[i * c:(i + 1) * c], wq, s, b, local[i * c:(i + 1) * c], ns)
+                dist.all_gather_into_tensor(blocks[i].view(self.world * c, ns), local[i * c:(i + 1) * c],
+                                            group=self.group)
+                gather_relayout(blocks[i], out[i * c:(i + 1) * c])
+            return out
+        cur = torch.cuda.current_stream(x.device)
+        comm = self._comm_stream(x.device)
+        comm.wait_stream(cur)  # out and the buffers are free once earlier work on the stream is done
+        for i in range(chunks):
+            self.local_op(x[i * c:(i + 1) * c], wq, s, b, local[i * c:(i + 1) * c], ns)
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev)
+                dist.all_gather_into_tensor(blocks[i].view(self.world * c, ns), local[i * c:(i + 1) * c],
+                                            group=self.group)
+                gather_relayout(blocks[i], out[i * c:(i + 1) * c])
+        cur.wait_stream(comm)
+        return out
 
     def forward(self, x, wq, s, b):
         k = x.shape[-1]

@@ -39,7 +39,14 @@ def _worker(rank, world, port, ret):
         y = op.forward(bf16.to_torch_bf16(x), ws, ss, bs)
         ref = qmm.qmm(x, wq, s, b)
         err = float(np.max(np.abs(y.float().numpy() - ref)))
-        ret[rank] = err <= 1e-2 * np.max(np.abs(ref))
+        ok = err <= 1e-2 * np.max(np.abs(ref))
+        # the chunked form (row blocks gathered one by one) gives the same output
+        x6 = gen.x_bf16(rng, 6, k)
+        yc = torch.empty(6, n, dtype=torch.bfloat16)
+        op.forward_into(bf16.to_torch_bf16(x6), ws, ss, bs, yc, chunks=3)
+        y1 = torch.empty(6, n, dtype=torch.bfloat16)
+        op.forward_into(bf16.to_torch_bf16(x6), ws, ss, bs, y1)
+        ret[rank] = ok and torch.equal(yc, y1)
     finally:
         dist.destroy_process_group()
 

@@ -1,7 +1,9 @@
-"""Tensor-parallel qmm with the output gathered inside the kernel
-(tsb_qmm_w4g64_gather), on 2, 4 and 8 GPUs: each rank's output holds every
-rank's columns, bit-identical to each shard's single-GPU result, across
-repeated calls into the same buffer, eager and replayed from a CUDA graph.
+"""Tensor-parallel qmm on 2, 4 and 8 GPUs. The verify path with the output
+gathered inside the kernel (tsb_qmm_w4g64_gather): each rank's output holds
+every rank's columns, bit-identical to each shard's single-GPU result, across
+repeated calls into the same buffer, eager and replayed from a CUDA graph. The
+prefill (M = 4096) with NCCL all-gathers overlapped against the row blocks'
+matmuls (ShardedQMM chunks): bit-identical likewise.
 
 Each world size needs that many GPUs (skipped otherwise): ranks that wait on
 one another never share a GPU."""
@@ -67,6 +69,20 @@ def _worker(rank, world, port, q):
                 if not torch.equal(out, ref):
                     errors.append(f"graph {m}x{n}x{k} rep {rep}")
             del graph
+        # prefill: N-sharded M = 4096, all-gathered block by block behind the compute
+        sq = tdist.ShardedQMM(world, rank)
+        for (m, n, k) in [(4096, 34816 // 8 * world, 5120), (4096, 5120 // 8 * world, 17408 // 4)]:
+            g = torch.Generator(device="cuda").manual_seed(2000 + n + k)
+            wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda", generator=g) * 0.02)
+            x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+            shards = [tdist.shard_weight(wq, s, b, world, r) for r in range(world)]
+            ref = torch.cat([ops.quantized_matmul(x, *sh) for sh in shards], dim=1)
+            for chunks in (1, 4):
+                out = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+                sq.forward_into(x, *shards[rank], out, chunks=chunks)
+                torch.cuda.synchronize()
+                if not torch.equal(out, ref):
+                    errors.append(f"prefill {m}x{n}x{k} chunks {chunks}")
         status = tsb._lib.load().tsb_device_status(None, 0)
         torch.cuda.synchronize()
         dist.barrier()
