@@ -118,8 +118,10 @@ int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const vo
  * TSB_ETIMEOUT (tsb_device_status). Before storing into a peer's y, a call
  * waits until that peer has started the same call, so work queued before it
  * on the peer's stream (readers of the old contents) has finished.
- * M <= 128 (the verify path; larger M: TSB_EUNSUPPORTED), ldy >= world*Ns;
- * workspace tsb_qmm_workspace_bytes(M, Ns, K); other rules as tsb_qmm_w4g64.
+ * Any M: M <= 128 runs the verify kernel, larger M the prefill GEMM, each
+ * storing its tiles into every rank's y as they complete (the transfer overlaps
+ * the matmul). ldy >= world*Ns; workspace tsb_qmm_workspace_bytes(M, Ns, K)
+ * (none past M = 128); other rules as tsb_qmm_w4g64.
  * ---------------------------------------------------------------------- */
 #define TSB_MAX_GATHER_RANKS 8
 typedef struct {

@@ -8,7 +8,7 @@ int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16
            int K, int ldy, void *ws, size_t ws_bytes, const GatherSpec *gs, cudaStream_t st);
 size_t qmm_ts_workspace_bytes(int M, int N, int K);
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-             int K, int ldy, cudaStream_t st);
+             int K, int ldy, const GatherSpec *gs, cudaStream_t st);
 
 // Rows above which the tcgen05 GEMM (dequantize into shared memory, 256-row
 // tiles) takes over from the verify-pass kernel (weights dequantized into
@@ -36,11 +36,12 @@ extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scale
     return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
                   ldy, ws, ws_bytes, nullptr, (cudaStream_t)stream);
   return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
-                  ldy, (cudaStream_t)stream);
+                  ldy, nullptr, (cudaStream_t)stream);
 }
 
 // Tensor-parallel form: this rank's N-shard, its output columns stored into
-// every rank's y by the kernel itself (no separate all-gather).
+// every rank's y by the kernel itself (no separate all-gather): the verify
+// kernel at M <= 128, the prefill GEMM above.
 extern "C" int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void *scales, const void *biases, int M,
                                     int Ns, int K, int ldy, const tsb_gather_t *g, void *ws, size_t ws_bytes,
                                     tsb_stream_t stream) {
@@ -48,7 +49,6 @@ extern "C" int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void
   if (g->world < 1 || g->world > TSB_MAX_GATHER_RANKS || g->rank < 0 || g->rank >= g->world) return TSB_EINVAL;
   if (M <= 0 || Ns <= 0 || K <= 0) return TSB_EINVAL;
   if (K % 64 || Ns % 128) return TSB_EUNSUPPORTED;
-  if (M > kTsMaxRows) return TSB_EUNSUPPORTED;
   if ((long long)ldy < (long long)Ns * g->world || ldy % 8) return TSB_EINVAL;
   if (!aligned(x, 16) || !aligned(w, 16)) return TSB_EINVAL;
   GatherSpec gs;
@@ -64,6 +64,11 @@ extern "C" int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void
     gs.y[p] = g->y[p];
     gs.sig[p] = g->sig[p];
   }
-  return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases,
-                (uint16_t *)g->y[g->rank] + gs.col0, M, Ns, K, ldy, ws, ws_bytes, &gs, (cudaStream_t)stream);
+  uint16_t *y_own = (uint16_t *)g->y[g->rank] + gs.col0;
+  if (M <= kTsMaxRows)
+    return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, y_own, M, Ns, K, ldy,
+                  ws, ws_bytes, &gs, (cudaStream_t)stream);
+  // prefill: the tcgen05 GEMM stores every tile into every rank's y
+  return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, y_own, M, Ns, K, ldy,
+                  &gs, (cudaStream_t)stream);
 }

@@ -18,14 +18,16 @@
 // the stage's `empty` barrier before it refills the codes the dequantizers
 // wait on).
 //
-// Dequantization per packed word (8 codes): per pair of codes one byte permute
-// and one mask leave them as bf16 integers times 2^-133 / 2^-129, and one bf16x2
-// fma with (s * 2^133, s * 2^129) rounds s*q + b once to bf16 (dequant_word_sub;
-// scales of 2^-5 and above take the magic-number form, dequant_word, with the
-// same result). The reference rounds q*s + b to float32 first
-// (qmm_packed.py:635); the two agree unless that float32 rounding lands exactly
-// on a bf16 rounding midpoint, never for quantizer-produced weights.
-#include "sm100.cuh"
+// Dequantization per packed word (8 codes): two masks and one shift split the
+// nibbles, byte permutes place code | 0x4300 (= bf16 128 + q) in natural order,
+// an exact bf16 subtract of 128 gives q, and one bf16x2 fma rounds s*q + b once
+// to bf16 (dequant_word). Here each thread dequantizes one word of each of its
+// rows, so the per-group scale-pair form of the verify kernel (dequant_word_sub)
+// would recompute its scale pair and branch per word; measured 23% slower at
+// M = 4096. The reference rounds q*s + b to float32 first (qmm_packed.py:635);
+// the two agree unless that float32 rounding lands exactly on a bf16 rounding
+// midpoint, never for quantizer-produced weights.
+#include "gather.cuh"
 
 namespace tsb {
 
@@ -47,11 +49,21 @@ struct GemmCfg {
   static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
 };
 
+// The output: yp[0] = y on one GPU; over `world` GPUs yp[p] is rank p's y at
+// this rank's first column and sig[p] its signal block (gather.cuh): every tile
+// is stored into every rank's y, so the N-sharded prefill needs no separate
+// all-gather.
+struct GemmOut {
+  int world, rank;
+  uint16_t *yp[kMaxGatherRanks];
+  uint32_t *sig[kMaxGatherRanks];
+};
+
 template <int BN>
 __global__ void __launch_bounds__(320, 1)
 qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                 const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases,
-                uint16_t *__restrict__ y, int M, int N, int K, int ldy) {
+                const GemmOut o, int M, int N, int K, int ldy) {
   using C = GemmCfg<BN>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -69,6 +81,10 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   const int G = K / 64;
   const int num_k = G;
 
+  // gathered output: this call's epoch (the previous kernel on the stream has
+  // completed); the first CTA tells the peers that this rank has started it
+  const uint32_t ep = o.world > 1 ? gather_epoch(o.sig, o.world, o.rank) : 0u;
+  if (o.world > 1 && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) gather_start(o.sig, o.world, o.rank, ep);
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_x[s], 1);
@@ -174,12 +190,8 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         const uint32_t w = codes[r * 8 + j];
         const uint32_t sbv = sb_cur[it];
         const __nv_bfloat162 b2 = u32_as_bf2((sbv >> 16) | (sbv & 0xFFFF0000u));
-        uint32_t o[4], sp;
-        if (sub_scale_pair(sbv & 0xFFFFu, sp)) {
-          dequant_word_sub(w, u32_as_bf2(sp), b2, o);
-        } else {  // scales of 2^-5 and above, subnormal, inf or nan
-          dequant_word(w, u32_as_bf2((sbv & 0xFFFFu) | (sbv << 16)), b2, o);
-        }
+        uint32_t o[4];
+        dequant_word(w, u32_as_bf2((sbv & 0xFFFFu) | (sbv << 16)), b2, o);
         const uint32_t off = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
         *reinterpret_cast<uint4 *>(btile + off) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -192,6 +204,8 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     // ---------------- epilogue
     if (ok && warp_wait(acc_full, 0)) {
       tc_fence_after();
+      // stores into a peer's y wait until that peer has started this call
+      if (o.world > 1) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
       const int q = warp & 3;                 // TMEM lane quadrant this warp may access
       const int half = (warp - 2) >> 2;       // which half of the columns
       for (int mh = 0; mh < 2; ++mh) {
@@ -204,9 +218,11 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
             uint32_t p[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) p[e] = pack_bf16x2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-            uint4 *dst = reinterpret_cast<uint4 *>(y + (size_t)row * ldy + n0 + c);
-            dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
-            dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+            for (int pp = 0; pp < o.world; ++pp) {
+              uint4 *dst = reinterpret_cast<uint4 *>(o.yp[pp] + (size_t)row * ldy + n0 + c);
+              dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+              dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
+            }
           }
         }
       }
@@ -219,11 +235,12 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (o.world > 1 && threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x * gridDim.y);
 }
 
 template <int BN>
 int launch_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-                int K, int ldy, cudaStream_t st) {
+                int K, int ldy, const GatherSpec *gs, cudaStream_t st) {
   using C = GemmCfg<BN>;
   CUtensorMap tx, tw;
   if (make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64, 128,
@@ -240,17 +257,31 @@ int launch_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const u
       return TSB_ECUDA;
     done = true;
   }
+  GemmOut o;
+  for (int p = 0; p < kMaxGatherRanks; ++p) { o.yp[p] = nullptr; o.sig[p] = nullptr; }
+  if (gs) {
+    o.world = gs->world;
+    o.rank = gs->rank;
+    for (int p = 0; p < gs->world; ++p) {
+      o.yp[p] = static_cast<uint16_t *>(gs->y[p]) + gs->col0;
+      o.sig[p] = gs->sig[p];
+    }
+  } else {
+    o.world = 1;
+    o.rank = 0;
+    o.yp[0] = y;
+  }
   dim3 grid((M + C::BM - 1) / C::BM, N / BN);
-  qmm_gemm_kernel<BN><<<grid, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, y, M, N, K, ldy);
+  qmm_gemm_kernel<BN><<<grid, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, o, M, N, K, ldy);
   return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 }  // namespace
 
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-             int K, int ldy, cudaStream_t st) {
-  if (N % 256 == 0) return launch_gemm<256>(x, w, s, b, y, M, N, K, ldy, st);
-  return launch_gemm<128>(x, w, s, b, y, M, N, K, ldy, st);
+             int K, int ldy, const GatherSpec *gs, cudaStream_t st) {
+  if (N % 256 == 0) return launch_gemm<256>(x, w, s, b, y, M, N, K, ldy, gs, st);
+  return launch_gemm<128>(x, w, s, b, y, M, N, K, ldy, gs, st);
 }
 
 unsigned int status_gemm(bool reset) {

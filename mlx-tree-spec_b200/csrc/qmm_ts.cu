@@ -64,7 +64,7 @@
 // quantizer-made scales and biases. tsb_dequant_w4g64 follows the reference's
 // two roundings bit for bit. The weights carry the bias, so each group costs
 // only its four K=16 MMAs.
-#include "sm100.cuh"
+#include "gather.cuh"
 
 #include <string.h>
 
@@ -144,42 +144,11 @@ struct TsArgs {
   long long U;
   int M, N, K, ldy, P, nst, maxp;
   // Output over `world` GPUs: yp[p] is rank p's y at this rank's first column
-  // (world 1: yp[0] is y). sig[p] is rank p's signal block: words [0, world)
-  // hold the epoch each rank last started; [world, 2 world) count the CTAs of
-  // each rank that have finished writing their part of y there (cumulative
-  // over calls); [2 world, 2 world + 3) are rank p's own counters (CTAs done
-  // in the current call, epoch, cumulative CTA total).
+  // (world 1: yp[0] is y); sig[p] is rank p's signal block (gather.cuh).
   int world, rank;
   uint16_t *yp[kMaxGatherRanks];
   uint32_t *sig[kMaxGatherRanks];
 };
-
-TSB_HD uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-TSB_HD void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-TSB_HD void red_add_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Bounded wait until every other rank's word `base + p` has reached value ep
-// (wrap-safe comparison); false (and TSB_ETIMEOUT recorded) if one does not.
-TSB_HD bool wait_peers(const uint32_t *base, int world, int rank, uint32_t ep) {
-  for (int p = 0; p < world; ++p) {
-    if (p == rank) continue;
-    const unsigned long long t0 = globaltimer_ns();
-    while ((int)(ld_acquire_sys(base + p) - ep) < 0) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        record_status(TSB_ETIMEOUT);
-        return false;
-      }
-    }
-  }
-  return true;
-}
 
 TSB_HD uint32_t ld_acquire_gpu(const uint32_t *p) {
   uint32_t v;
@@ -505,10 +474,8 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     uint32_t ep = 0;
     bool peers_started = a.world == 1;
     if (a.world > 1) {
-      ep = *reinterpret_cast<volatile uint32_t *>(a.sig[a.rank] + 2 * a.world + 1) + 1u;
-      if (c == 0 && threadIdx.x == 0)
-        for (int pp = 0; pp < a.world; ++pp)
-          if (pp != a.rank) st_release_sys(a.sig[pp] + a.rank, ep);
+      ep = gather_epoch(a.sig, a.world, a.rank);
+      if (c == 0 && threadIdx.x == 0) gather_start(a.sig, a.world, a.rank, ep);
     }
     int li = 0, seg = 0;
     int tile, st0;
@@ -658,25 +625,7 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
-  if (a.world > 1 && threadIdx.x == 0) {
-    // Every CTA counts itself done in each peer's block with a system-scope
-    // release (cumulative: it orders this CTA's peer stores, which the barrier
-    // above ordered before it); the CTAs release in parallel as they finish.
-    // The last CTA of this rank then waits until every peer's count has
-    // reached this rank's own running total (every rank makes the same calls
-    // with the same grid), so y is complete on every rank when the grid
-    // completes.
-    uint32_t *own = a.sig[a.rank];
-    for (int pp = 0; pp < a.world; ++pp)
-      if (pp != a.rank) red_add_release_sys(a.sig[pp] + a.world + a.rank, 1u);
-    if (atomicAdd(own + 2 * a.world, 1u) + 1u == gridDim.x) {
-      own[2 * a.world] = 0u;
-      const uint32_t total = own[2 * a.world + 2] + gridDim.x;
-      wait_peers(own + a.world, a.world, a.rank, total);
-      own[2 * a.world + 2] = total;
-      own[2 * a.world + 1] += 1u;  // this call's epoch is complete on this rank
-    }
-  }
+  if (a.world > 1 && threadIdx.x == 0) gather_finish(a.sig, a.world, a.rank, gridDim.x);
 }
 
 // The workspace starts with a fixed flag region for every shape: partials of

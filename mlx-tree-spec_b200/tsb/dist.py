@@ -8,12 +8,15 @@ each rank computes its (M, N/G) slice and every rank ends with the full
 (M, N) output.
 
 Two forms:
-  GatheredQMM  the verify path (M <= 128): one kernel per rank computes its
-               slice and stores it into every rank's output over NVLink (peer
-               memory from torch symmetric memory), exchanging completion
-               flags itself (tsb_qmm_w4g64_gather); no separate collective.
-  ShardedQMM   any M: the shard's matmul, then one NCCL all-gather and a
-               relayout into the caller's buffer.
+  GatheredQMM  any M: one kernel per rank (the verify kernel at M <= 128, the
+               prefill GEMM above) computes its slice and stores each finished
+               tile into every rank's output over NVLink (peer memory from
+               torch symmetric memory), exchanging completion flags itself
+               (tsb_qmm_w4g64_gather): the transfer overlaps the matmul and no
+               separate collective runs.
+  ShardedQMM   any M: the shard's matmul, then NCCL all-gathers and a
+               relayout into the caller's buffer (optionally block by block of
+               rows, overlapped with the next block's matmul).
 
 Every rank takes the same collective steps in the same order.
 """

@@ -100,8 +100,8 @@ def test_gather_and_decoder_checks_before_any_launch(lib_built):
     assert gather(x=None) == _lib.TSB_EINVAL
     assert gather(gg=None) == _lib.TSB_EINVAL
     assert gather(ns=1000) == _lib.TSB_EUNSUPPORTED  # shard rows not a multiple of 128
-    assert gather(m=129) == _lib.TSB_EUNSUPPORTED    # the verify path only
     assert gather(ldy=1024) == _lib.TSB_EINVAL       # narrower than world * Ns
+    assert gather(m=4096, ldy=1024) == _lib.TSB_EINVAL  # the prefill form checks the same
     bad = _lib.GatherT()
     bad.world, bad.rank = 2, 2
     assert gather(gg=bad) == _lib.TSB_EINVAL         # rank out of range

@@ -1,9 +1,10 @@
-"""Tensor-parallel qmm on 2, 4 and 8 GPUs. The verify path with the output
-gathered inside the kernel (tsb_qmm_w4g64_gather): each rank's output holds
-every rank's columns, bit-identical to each shard's single-GPU result, across
-repeated calls into the same buffer, eager and replayed from a CUDA graph. The
-prefill (M = 4096) with NCCL all-gathers overlapped against the row blocks'
-matmuls (ShardedQMM chunks): bit-identical likewise.
+"""Tensor-parallel qmm on 2, 4 and 8 GPUs. The output gathered inside the
+kernel (tsb_qmm_w4g64_gather; the verify kernel and, past M = 128, the prefill
+GEMM): each rank's output holds every rank's columns, bit-identical to each
+shard's single-GPU result, across repeated calls into the same buffer, eager
+and replayed from a CUDA graph. The prefill (M = 4096) with NCCL all-gathers
+overlapped against the row blocks' matmuls (ShardedQMM chunks): bit-identical
+likewise.
 
 Each world size needs that many GPUs (skipped otherwise): ranks that wait on
 one another never share a GPU."""
@@ -41,7 +42,8 @@ def _worker(rank, world, port, q):
                                 device_id=torch.device("cuda", rank))
         gq = tdist.GatheredQMM(world, rank)
         errors = []
-        for (m, n, k) in [(16, 6144, 5120), (1, 1024, 1024), (64, 2048, 2560), (128, 1024, 640), (33, 3072, 1536)]:
+        for (m, n, k) in [(16, 6144, 5120), (1, 1024, 1024), (64, 2048, 2560), (128, 1024, 640), (33, 3072, 1536),
+                          (4096, 34816 // 8 * world, 5120), (300, 1024, 640)]:
             g = torch.Generator(device="cuda").manual_seed(1000 + m + n)
             wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda", generator=g) * 0.02)
             x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
