@@ -8,7 +8,8 @@ int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16
            int K, int ldy, void *ws, size_t ws_bytes, const GatherSpec *gs, cudaStream_t st);
 size_t qmm_ts_workspace_bytes(int M, int N, int K);
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-             int K, int ldy, const GatherSpec *gs, cudaStream_t st);
+             int K, int ldy, const GatherSpec *gs, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t qmm_gemm_workspace_bytes(int M, int N, int K);
 
 // Rows above which the tcgen05 GEMM (dequantize into shared memory, 256-row
 // tiles) takes over from the verify-pass kernel (weights dequantized into
@@ -19,10 +20,11 @@ constexpr int kTsMaxRows = 128;
 using namespace tsb;
 
 // The verify path (M <= 128) needs completion flags and the float partials of
-// the row tiles it splits across CTAs; the prefill GEMM needs nothing.
+// the row tiles it splits across CTAs; the prefill GEMM the float sums of its
+// split tail, if it has one.
 extern "C" size_t tsb_qmm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || N % 128 || K % 64) return 0;
-  return M <= kTsMaxRows ? qmm_ts_workspace_bytes(M, N, K) : 0;
+  return M <= kTsMaxRows ? qmm_ts_workspace_bytes(M, N, K) : qmm_gemm_workspace_bytes(M, N, K);
 }
 
 extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const void *biases, void *y,
@@ -36,7 +38,7 @@ extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scale
     return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
                   ldy, ws, ws_bytes, nullptr, (cudaStream_t)stream);
   return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N, K,
-                  ldy, nullptr, (cudaStream_t)stream);
+                  ldy, nullptr, ws, ws_bytes, (cudaStream_t)stream);
 }
 
 // Tensor-parallel form: this rank's N-shard, its output columns stored into
@@ -70,5 +72,5 @@ extern "C" int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void
                   ws, ws_bytes, &gs, (cudaStream_t)stream);
   // prefill: the tcgen05 GEMM stores every tile into every rank's y
   return qmm_gemm((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, y_own, M, Ns, K, ldy,
-                  &gs, (cudaStream_t)stream);
+                  &gs, ws, ws_bytes, (cudaStream_t)stream);
 }

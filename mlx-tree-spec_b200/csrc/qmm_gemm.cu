@@ -33,6 +33,11 @@ namespace tsb {
 
 namespace {
 
+// The split tail's float sums start this far into the qmm workspace (after the
+// verify path's count region, which stays untouched and zero; the sums region
+// is zeroed by each call before use).
+constexpr size_t kGemmPartOffset = 64 * 1024;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 256;
@@ -59,11 +64,25 @@ struct GemmOut {
   uint32_t *sig[kMaxGatherRanks];
 };
 
+// Which tiles a launch covers: CTA b takes linear tile tile0 + b / ksplit
+// (M-tile fastest, so consecutive CTAs share a weight tile) and the K range
+// [j num_k / ksplit, (j+1) num_k / ksplit) with j = b % ksplit. ksplit = 1: the
+// whole tile, written to y (every rank's y when gathered); such a launch also
+// zeroes part[0 .. part_floats) for the split launch after it. ksplit > 1: float
+// partial sums added into part[b / ksplit] once the zeroing launch before it
+// has completed (the tail kernel below finishes those tiles). The workspace may
+// hold anything on entry (the verify path leaves its float partials there).
+struct GemmTiles {
+  int tile0, mtiles, ksplit;
+  float *part;
+  long long part_floats;
+};
+
 template <int BN>
 __global__ void __launch_bounds__(320, 1)
 qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                 const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases,
-                const GemmOut o, int M, int N, int K, int ldy) {
+                const GemmOut o, const GemmTiles tl, int M, int N, int K, int ldy) {
   using C = GemmCfg<BN>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -76,15 +95,22 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4 * C::STAGES + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m0 = blockIdx.x * C::BM;
-  const int n0 = blockIdx.y * BN;
+  const int tidx = blockIdx.x / tl.ksplit, kpart = blockIdx.x % tl.ksplit;
+  const int tile = tl.tile0 + tidx;
+  const int m0 = (tile % tl.mtiles) * C::BM;
+  const int n0 = (tile / tl.mtiles) * BN;
   const int G = K / 64;
-  const int num_k = G;
+  const int k0 = (int)((long long)G * kpart / tl.ksplit), k1 = (int)((long long)G * (kpart + 1) / tl.ksplit);
+  const int num_k = k1 - k0;  // K steps of this CTA: i in [k0, k1), ring position i - k0
+  const bool partial = tl.ksplit > 1;
+  const bool gathered = o.world > 1 && !partial;
 
+  // the next kernel of the call (the split tail) may start as this one's CTAs exit
+  if (threadIdx.x == 0) griddep_launch_dependents();
   // gathered output: this call's epoch (the previous kernel on the stream has
   // completed); the first CTA tells the peers that this rank has started it
-  const uint32_t ep = o.world > 1 ? gather_epoch(o.sig, o.world, o.rank) : 0u;
-  if (o.world > 1 && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) gather_start(o.sig, o.world, o.rank, ep);
+  const uint32_t ep = gathered ? gather_epoch(o.sig, o.world, o.rank) : 0u;
+  if (gathered && blockIdx.x == 0 && threadIdx.x == 0) gather_start(o.sig, o.world, o.rank, ep);
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_x[s], 1);
@@ -119,11 +145,12 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           if (!mbar_wait(&empty[s], ((i / C::STAGES) - 1) & 1)) break;
         }
         unsigned char *st = stage_ptr(s);
+        const int kc = (k0 + i) * C::BK;
         mbar_arrive_expect_tx(&full_x[s], 2 * C::A_BYTES);
-        tma_load_2d(st, &tmap_x, i * C::BK, m0, &full_x[s]);
-        tma_load_2d(st + C::A_BYTES, &tmap_x, i * C::BK, m0 + 128, &full_x[s]);
+        tma_load_2d(st, &tmap_x, kc, m0, &full_x[s]);
+        tma_load_2d(st + C::A_BYTES, &tmap_x, kc, m0 + 128, &full_x[s]);
         mbar_arrive_expect_tx(&full_c[s], C::C_BYTES);
-        tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &tmap_w, i * 8, n0, &full_c[s]);
+        tma_load_2d(st + 2 * C::A_BYTES + C::B_BYTES, &tmap_w, (k0 + i) * 8, n0, &full_c[s]);
         issued = i + 1;
       }
       // drain: every issued load has landed before the CTA can exit
@@ -164,6 +191,12 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   } else {
     // ---------------- dequantizers, then epilogue
     const int t = threadIdx.x - 64;  // 0..255
+    if (!partial && tl.part) {
+      // this CTA's slice of the split tail's sums, zeroed for the split launch
+      const long long per = ((tl.part_floats / gridDim.x + 4) / 4) * 4;
+      const long long a0 = per * blockIdx.x, a1 = min(a0 + per, tl.part_floats);
+      for (long long e = a0 + 4 * t; e < a1; e += 4 * C::DQ_THREADS) st_cg_zero_v4(tl.part + e);
+    }
     const int j = t & 7;             // word within the group
     const int rsub = t >> 3;         // 0..31
     uint32_t sb_cur[C::ROWS_PER_DQ], sb_nxt[C::ROWS_PER_DQ];  // (s | b << 16)
@@ -174,12 +207,12 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         dst[it] = uint32_t(__ldg(scales + idx)) | (uint32_t(__ldg(biases + idx)) << 16);
       }
     };
-    load_sb(0, sb_cur);
+    load_sb(k0, sb_cur);
     bool ok = true;
     for (int i = 0; i < num_k; ++i) {
       const int s = i % C::STAGES;
       const uint32_t par = (i / C::STAGES) & 1;
-      if (i + 1 < num_k) load_sb(i + 1, sb_nxt);
+      if (i + 1 < num_k) load_sb(k0 + i + 1, sb_nxt);
       if (!warp_wait(&full_c[s], par)) { ok = false; break; }
       unsigned char *st = stage_ptr(s);
       const uint32_t *codes = reinterpret_cast<const uint32_t *>(st + 2 * C::A_BYTES + C::B_BYTES);
@@ -205,7 +238,10 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     if (ok && warp_wait(acc_full, 0)) {
       tc_fence_after();
       // stores into a peer's y wait until that peer has started this call
-      if (o.world > 1) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
+      if (gathered) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
+      // split: the sums are zeroed by the whole-tile launch before this one
+      if (partial) griddep_wait();
+      float *pt = partial ? tl.part + (size_t)tidx * C::BM * BN : nullptr;
       const int q = warp & 3;                 // TMEM lane quadrant this warp may access
       const int half = (warp - 2) >> 2;       // which half of the columns
       for (int mh = 0; mh < 2; ++mh) {
@@ -214,7 +250,13 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           uint32_t r[16];
           tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(mh * BN + c), r);
           tmem_wait_ld();
-          if (row < M) {
+          if (row < M && partial) {
+            float *dst = pt + (size_t)(row - m0) * BN + c;  // this K range's sums, added at L2
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              red_add_v4(dst + e, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                         __uint_as_float(r[e + 3]));
+          } else if (row < M) {
             uint32_t p[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) p[e] = pack_bf16x2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
@@ -235,12 +277,75 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
-  if (o.world > 1 && threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x * gridDim.y);
+  if (gathered && threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x);
+}
+
+// Finishes the tiles of a split tail: sums (float, [tiles][256][BN]) -> bf16 y
+// (every rank's y when gathered). One CTA per 128 rows of a tile, thread = row,
+// 8 columns per step. Its wait for the split launch also covers the whole-tile
+// launch: the split launch's epilogues waited for that one.
+template <int BN>
+__global__ void __launch_bounds__(128)
+qmm_gemm_tail_kernel(float *part, int tile0, int mtiles, const GemmOut o, int M, int ldy) {
+  griddep_wait();  // the partial sums of the previous kernel are complete
+  const int ti = blockIdx.x >> 1, half = blockIdx.x & 1;
+  const int tile = tile0 + ti;
+  const int m0 = (tile % mtiles) * 256, n0 = (tile / mtiles) * BN;
+  const int rt = half * 128 + threadIdx.x, row = m0 + rt;
+  const bool gathered = o.world > 1;
+  const uint32_t ep = gathered ? gather_epoch(o.sig, o.world, o.rank) : 0u;
+  if (gathered && blockIdx.x == 0 && threadIdx.x == 0) gather_start(o.sig, o.world, o.rank, ep);
+  if (gathered) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
+  if (row < M) {
+    float *src = part + ((size_t)ti * 256 + rt) * BN;
+    for (int c = 0; c < BN; c += 8) {
+      const float4 a = ld_cg_v4(src + c), b = ld_cg_v4(src + c + 4);
+      const uint4 v = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                                 pack_bf16x2(b.z, b.w));
+      for (int pp = 0; pp < o.world; ++pp)
+        *reinterpret_cast<uint4 *>(o.yp[pp] + (size_t)row * ldy + n0 + c) = v;
+    }
+  }
+  __syncthreads();
+  if (gathered && threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x);
+}
+
+// The split tail: when the tiles fill the SMs' last wave poorly (e.g. 320 tiles of
+// 256 x 256 at M = 4096, N = 5120 leave 24 tiles for a third wave of 148 SMs),
+// the full waves run as usual and the remaining tiles are split along K over the
+// SMs (float sums added at L2 into the workspace), then finished by the tail
+// kernel. tail = 0: one launch.
+struct GemmPlan {
+  int mtiles, tiles, full, tail, ksplit;
+};
+
+template <int BN>
+GemmPlan plan_gemm(int M, int N, int K) {
+  GemmPlan p;
+  p.mtiles = (M + 255) / 256;
+  p.tiles = p.mtiles * (N / BN);
+  const int sms = sm_count();
+  const int rem = p.tiles % sms;
+  const int steps = K / 64;
+  p.full = p.tiles;
+  p.tail = 0;
+  p.ksplit = 1;
+  if (p.tiles >= sms && rem > 0 && 2 * rem <= sms) {
+    int ks = sms / rem;
+    if (ks > 16) ks = 16;
+    if (ks > steps / 4) ks = steps / 4;
+    if (ks >= 3) {  // a 2-way split of a half-empty wave measured slower than none
+      p.full = p.tiles - rem;
+      p.tail = rem;
+      p.ksplit = ks;
+    }
+  }
+  return p;
 }
 
 template <int BN>
 int launch_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-                int K, int ldy, const GatherSpec *gs, cudaStream_t st) {
+                int K, int ldy, const GatherSpec *gs, void *ws, size_t ws_bytes, cudaStream_t st) {
   using C = GemmCfg<BN>;
   CUtensorMap tx, tw;
   if (make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, 64, 128,
@@ -271,17 +376,61 @@ int launch_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const u
     o.rank = 0;
     o.yp[0] = y;
   }
-  dim3 grid((M + C::BM - 1) / C::BM, N / BN);
-  qmm_gemm_kernel<BN><<<grid, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, o, M, N, K, ldy);
-  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+  GemmPlan pl = plan_gemm<BN>(M, N, K);
+  // the split tail keeps its sums in the workspace (after the verify path's
+  // count region, whatever the region holds); without one, every tile runs whole
+  float *part = nullptr;
+  if (pl.tail) {
+    const size_t need = kGemmPartOffset + (size_t)pl.tail * 256 * BN * sizeof(float);
+    if (ws && ws_bytes >= need && aligned(ws, 256))
+      part = reinterpret_cast<float *>(static_cast<unsigned char *>(ws) + kGemmPartOffset);
+    else
+      pl.full = pl.tiles, pl.tail = 0, pl.ksplit = 1;
+  }
+  GemmTiles whole{0, pl.mtiles, 1, part, (long long)pl.tail * 256 * BN};
+  qmm_gemm_kernel<BN><<<pl.full, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, o, whole, M, N, K, ldy);
+  if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
+  if (!pl.tail) return TSB_OK;
+  // the tail starts on SMs as the last full wave's CTAs exit (it touches
+  // nothing the full tiles write)
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.stream = st;
+  cfg.gridDim = dim3(pl.tail * pl.ksplit, 1, 1);
+  cfg.blockDim = dim3(C::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  GemmTiles split{pl.full, pl.mtiles, pl.ksplit, part, 0};
+  if (cudaLaunchKernelEx(&cfg, qmm_gemm_kernel<BN>, tx, tw, s, b, o, split, M, N, K, ldy) != cudaSuccess)
+    return TSB_ECUDA;
+  cfg.gridDim = dim3(pl.tail * 2, 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  if (cudaLaunchKernelEx(&cfg, qmm_gemm_tail_kernel<BN>, part, pl.full, pl.mtiles, o, M, ldy) != cudaSuccess)
+    return TSB_ECUDA;
+  return TSB_OK;
 }
 
 }  // namespace
 
 int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
-             int K, int ldy, const GatherSpec *gs, cudaStream_t st) {
-  if (N % 256 == 0) return launch_gemm<256>(x, w, s, b, y, M, N, K, ldy, gs, st);
-  return launch_gemm<128>(x, w, s, b, y, M, N, K, ldy, gs, st);
+             int K, int ldy, const GatherSpec *gs, void *ws, size_t ws_bytes, cudaStream_t st) {
+  if (N % 256 == 0) return launch_gemm<256>(x, w, s, b, y, M, N, K, ldy, gs, ws, ws_bytes, st);
+  return launch_gemm<128>(x, w, s, b, y, M, N, K, ldy, gs, ws, ws_bytes, st);
+}
+
+// Workspace of the prefill path: the split tail's sums (0 when the tiles fill
+// the last wave well).
+size_t qmm_gemm_workspace_bytes(int M, int N, int K) {
+  if (N % 256 == 0) {
+    const GemmPlan p = plan_gemm<256>(M, N, K);
+    return p.tail ? kGemmPartOffset + (size_t)p.tail * 256 * 256 * sizeof(float) : 0;
+  }
+  const GemmPlan p = plan_gemm<128>(M, N, K);
+  return p.tail ? kGemmPartOffset + (size_t)p.tail * 256 * 128 * sizeof(float) : 0;
 }
 
 unsigned int status_gemm(bool reset) {

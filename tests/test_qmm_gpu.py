@@ -293,3 +293,37 @@ def test_effective_weights_rounding_rule(m):
         for i in range(m):
             got[:, (k0 + i) % k] = y[i]
     assert np.array_equal(got, once), int(np.sum(got != once))
+
+
+@pytest.mark.parametrize("m,n,k", [(1100, 7680, 1024), (4096, 5120, 1536)])
+def test_qmm_gemm_split_tail(m, n, k):
+    """Prefill shapes whose tiles fill the SMs' last wave poorly: the last tiles
+    are split along K (float sums in the workspace, finished by a third
+    kernel). Full oracle check twice, the second time over a workspace whose
+    sums region holds garbage (the verify path leaves its partials there: the
+    prefill zeroes what it uses), and the same result within tolerance when no
+    workspace is given (every tile whole)."""
+    import tsb
+    from tsb import _lib, ops
+
+    rng = np.random.default_rng(8800 + m + n + k)
+    x = gen.x_bf16(rng, m, k)
+    wq, s, b = gen.weights_w4g64(rng, n, k)
+    lib = _lib.load()
+    nbytes = lib.tsb_qmm_workspace_bytes(m, n, k)
+    assert nbytes > 64 * 1024  # a split tail on this device (148 SMs)
+    ref = qmm.qmm(x, wq, s, b)
+    y = _run(x, wq, s, b)
+    assert_close_rel(y, ref, REL_TIGHT, f"split tail {m}x{n}x{k}")
+    ws = ops.qmm_workspace(nbytes, "cuda")
+    ws[64 * 1024:nbytes].fill_(0x7F)  # float 3.4e38 in every word of the sums region
+    y = _run(x, wq, s, b)
+    ws[64 * 1024:nbytes].zero_()
+    assert_close_rel(y, ref, REL_TIGHT, f"split tail over garbage {m}x{n}x{k}")
+    assert not torch.any(ws[:64 * 1024]).item(), "count region left non-zero"
+    xd, wd, sd, bd = dev_bf16(x), dev_u32(wq), dev_bf16(s), dev_bf16(b)
+    y0 = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    st = lib.tsb_qmm_w4g64(xd.data_ptr(), wd.data_ptr(), sd.data_ptr(), bd.data_ptr(), y0.data_ptr(), m, n, k, n,
+                           None, 0, torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    assert_close_rel(host_f32(y0), ref, REL_TIGHT, "no workspace")
