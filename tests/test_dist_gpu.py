@@ -43,7 +43,7 @@ def _worker(rank, world, port, q):
         gq = tdist.GatheredQMM(world, rank)
         errors = []
         for (m, n, k) in [(16, 6144, 5120), (1, 1024, 1024), (64, 2048, 2560), (128, 1024, 640), (33, 3072, 1536),
-                          (4096, 34816 // 8 * world, 5120), (300, 1024, 640)]:
+                          (4096, 34816 // 8 * world, 5120), (300, 1024, 640), (4096, 2560 * world, 1024)]:
             g = torch.Generator(device="cuda").manual_seed(1000 + m + n)
             wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda", generator=g) * 0.02)
             x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
