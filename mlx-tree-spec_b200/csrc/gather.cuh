@@ -49,18 +49,12 @@ TSB_HD bool wait_peers(const uint32_t *base, int world, int rank, uint32_t ep) {
   return true;
 }
 
-// Four floats added at L2 (one 16-byte reduction; the address is 16-byte aligned).
-TSB_HD void red_add_v4(float *p, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
-}
+// Four floats read through L2 (written by another grid of the stream).
 TSB_HD float4 ld_cg_v4(const float *p) {
   float4 v;
   asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p)
                : "memory");
   return v;
-}
-TSB_HD void st_cg_zero_v4(float *p) {
-  asm volatile("st.global.cg.v4.f32 [%0], {%1, %1, %1, %1};" ::"l"(p), "f"(0.f) : "memory");
 }
 
 // This call's epoch (read once the previous call on the stream has completed).

@@ -33,9 +33,8 @@ namespace tsb {
 
 namespace {
 
-// The split tail's float sums start this far into the qmm workspace (after the
-// verify path's count region, which stays untouched and zero; the sums region
-// is zeroed by each call before use).
+// The split tail's float parts start this far into the qmm workspace (after the
+// verify path's count region, which stays untouched and zero).
 constexpr size_t kGemmPartOffset = 64 * 1024;
 
 template <int BN>
@@ -67,15 +66,13 @@ struct GemmOut {
 // Which tiles a launch covers: CTA b takes linear tile tile0 + b / ksplit
 // (M-tile fastest, so consecutive CTAs share a weight tile) and the K range
 // [j num_k / ksplit, (j+1) num_k / ksplit) with j = b % ksplit. ksplit = 1: the
-// whole tile, written to y (every rank's y when gathered); such a launch also
-// zeroes part[0 .. part_floats) for the split launch after it. ksplit > 1: float
-// partial sums added into part[b / ksplit] once the zeroing launch before it
-// has completed (the tail kernel below finishes those tiles). The workspace may
-// hold anything on entry (the verify path leaves its float partials there).
+// whole tile, written to y (every rank's y when gathered). ksplit > 1: the
+// range's float sums stored into part[b] ([256][BN] per CTA); the tail kernel
+// below adds a tile's ksplit parts in a fixed order (deterministic results) and
+// writes y. The workspace may hold anything on entry.
 struct GemmTiles {
   int tile0, mtiles, ksplit;
   float *part;
-  long long part_floats;
 };
 
 template <int BN>
@@ -191,12 +188,6 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   } else {
     // ---------------- dequantizers, then epilogue
     const int t = threadIdx.x - 64;  // 0..255
-    if (!partial && tl.part) {
-      // this CTA's slice of the split tail's sums, zeroed for the split launch
-      const long long per = ((tl.part_floats / gridDim.x + 4) / 4) * 4;
-      const long long a0 = per * blockIdx.x, a1 = min(a0 + per, tl.part_floats);
-      for (long long e = a0 + 4 * t; e < a1; e += 4 * C::DQ_THREADS) st_cg_zero_v4(tl.part + e);
-    }
     const int j = t & 7;             // word within the group
     const int rsub = t >> 3;         // 0..31
     uint32_t sb_cur[C::ROWS_PER_DQ], sb_nxt[C::ROWS_PER_DQ];  // (s | b << 16)
@@ -234,37 +225,66 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
 #pragma unroll
       for (int it = 0; it < C::ROWS_PER_DQ; ++it) sb_cur[it] = sb_nxt[it];
     }
-    // ---------------- epilogue
-    if (ok && warp_wait(acc_full, 0)) {
-      tc_fence_after();
-      // stores into a peer's y wait until that peer has started this call
-      if (gathered) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
-      // split: the sums are zeroed by the whole-tile launch before this one
-      if (partial) griddep_wait();
-      float *pt = partial ? tl.part + (size_t)tidx * C::BM * BN : nullptr;
+    // ---------------- epilogue. Every epilogue warp goes through it, even after
+    // a failed (timed-out) wait, so that the named barrier below always
+    // completes; only the stores depend on success.
+    const bool good = warp_wait(acc_full, 0) && ok;
+    tc_fence_after();
+    // stores into a peer's y wait until that peer has started this call
+    if (good && gathered) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
+    {
       const int q = warp & 3;                 // TMEM lane quadrant this warp may access
       const int half = (warp - 2) >> 2;       // which half of the columns
-      for (int mh = 0; mh < 2; ++mh) {
-        const int row = m0 + mh * 128 + q * 32 + lane;
-        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(mh * BN + c), r);
-          tmem_wait_ld();
-          if (row < M && partial) {
-            float *dst = pt + (size_t)(row - m0) * BN + c;  // this K range's sums, added at L2
+      if (partial && good) {
+        // this K range's float sums, stored as they are read
+        float *pt = tl.part + (size_t)blockIdx.x * C::BM * BN;
+        for (int mh = 0; mh < 2; ++mh) {
+          const int row = m0 + mh * 128 + q * 32 + lane;
+          for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+            uint32_t r[16];
+            tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(mh * BN + c), r);
+            tmem_wait_ld();
+            if (row < M) {
+              float4 *dst = reinterpret_cast<float4 *>(pt + (size_t)(row - m0) * BN + c);
 #pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              red_add_v4(dst + e, __uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
-                         __uint_as_float(r[e + 3]));
-          } else if (row < M) {
+              for (int e = 0; e < 4; ++e)
+                dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                     __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+            }
+          }
+        }
+      } else if (!partial) {
+        // bf16 tile staged in shared memory (the pipeline's stages are free:
+        // every MMA has completed), then written out as whole rows, 16 bytes a
+        // thread, so that a warp's stores to y (a peer's y over NVLink) are
+        // contiguous runs of 256 or 512 bytes
+        constexpr int PITCH = BN * 2 + 16;    // staged row pitch: +16 B keeps 16-byte stores conflict-free
+        static_assert(C::BM * PITCH <= C::STAGES * C::STAGE_BYTES, "staging tile");
+        unsigned char *stg = smem;
+        fence_proxy_async_smem();
+        for (int mh = 0; mh < 2; ++mh) {
+          const int rr = mh * 128 + q * 32 + lane;
+          for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+            uint32_t r[16];
+            tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(mh * BN + c), r);
+            tmem_wait_ld();
             uint32_t p[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) p[e] = pack_bf16x2(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
-            for (int pp = 0; pp < o.world; ++pp) {
-              uint4 *dst = reinterpret_cast<uint4 *>(o.yp[pp] + (size_t)row * ldy + n0 + c);
-              dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
-              dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
-            }
+            uint4 *d = reinterpret_cast<uint4 *>(stg + rr * PITCH + c * 2);
+            d[0] = make_uint4(p[0], p[1], p[2], p[3]);
+            d[1] = make_uint4(p[4], p[5], p[6], p[7]);
+          }
+        }
+        named_barrier_sync(1, C::DQ_THREADS);
+        constexpr int CPR = BN / 8;           // 16-byte chunks per row
+        for (int i = t; i < C::BM * CPR; i += C::DQ_THREADS) {
+          const int rr = i / CPR, ch = i % CPR;
+          const int row = m0 + rr;
+          if (good && row < M) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(stg + rr * PITCH + ch * 16);
+            for (int pp = 0; pp < o.world; ++pp)
+              *reinterpret_cast<uint4 *>(o.yp[pp] + (size_t)row * ldy + n0 + ch * 8) = v;
           }
         }
       }
@@ -278,33 +298,44 @@ qmm_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if (gathered && threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x);
+  // a split launch starts before the whole-tile launch completes; it completes
+  // only after it, so that the tail kernel (which waits for this grid) and its
+  // gather handshakes come after both
+  if (partial) griddep_wait();
 }
 
-// Finishes the tiles of a split tail: sums (float, [tiles][256][BN]) -> bf16 y
-// (every rank's y when gathered). One CTA per 128 rows of a tile, thread = row,
-// 8 columns per step. Its wait for the split launch also covers the whole-tile
-// launch: the split launch's epilogues waited for that one.
+// Finishes the tiles of a split tail: the ksplit float parts of each tile
+// ([tiles][ksplit][256][BN]), added in order, -> bf16 y (every rank's y when
+// gathered). Thread = 8 columns of one row: a warp reads and writes contiguous
+// row segments; BN / 8 CTAs of 256 threads per tile.
 template <int BN>
-__global__ void __launch_bounds__(128)
-qmm_gemm_tail_kernel(float *part, int tile0, int mtiles, const GemmOut o, int M, int ldy) {
-  griddep_wait();  // the partial sums of the previous kernel are complete
-  const int ti = blockIdx.x >> 1, half = blockIdx.x & 1;
+__global__ void __launch_bounds__(256)
+qmm_gemm_tail_kernel(const float *part, int tile0, int mtiles, int ksplit, const GemmOut o, int M, int ldy) {
+  griddep_wait();  // the parts written by the previous kernel are complete
+  constexpr int CPR = BN / 8;  // 8-column chunks per row
+  const int ti = blockIdx.x / CPR;
+  const int i = (blockIdx.x % CPR) * 256 + threadIdx.x;  // (row, chunk) item of the tile
+  const int rr = i / CPR, ch = i % CPR;
   const int tile = tile0 + ti;
   const int m0 = (tile % mtiles) * 256, n0 = (tile / mtiles) * BN;
-  const int rt = half * 128 + threadIdx.x, row = m0 + rt;
+  const int row = m0 + rr;
   const bool gathered = o.world > 1;
   const uint32_t ep = gathered ? gather_epoch(o.sig, o.world, o.rank) : 0u;
   if (gathered && blockIdx.x == 0 && threadIdx.x == 0) gather_start(o.sig, o.world, o.rank, ep);
   if (gathered) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
   if (row < M) {
-    float *src = part + ((size_t)ti * 256 + rt) * BN;
-    for (int c = 0; c < BN; c += 8) {
-      const float4 a = ld_cg_v4(src + c), b = ld_cg_v4(src + c + 4);
-      const uint4 v = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
-                                 pack_bf16x2(b.z, b.w));
-      for (int pp = 0; pp < o.world; ++pp)
-        *reinterpret_cast<uint4 *>(o.yp[pp] + (size_t)row * ldy + n0 + c) = v;
+    const float *src = part + ((size_t)ti * ksplit * 256 + rr) * BN + ch * 8;
+    float4 a = ld_cg_v4(src), b = ld_cg_v4(src + 4);
+    for (int j = 1; j < ksplit; ++j) {
+      const float *q = src + (size_t)j * 256 * BN;
+      const float4 a2 = ld_cg_v4(q), b2 = ld_cg_v4(q + 4);
+      a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
+      b.x += b2.x; b.y += b2.y; b.z += b2.z; b.w += b2.w;
     }
+    const uint4 v = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                               pack_bf16x2(b.z, b.w));
+    for (int pp = 0; pp < o.world; ++pp)
+      *reinterpret_cast<uint4 *>(o.yp[pp] + (size_t)row * ldy + n0 + ch * 8) = v;
   }
   __syncthreads();
   if (gathered && threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x);
@@ -313,8 +344,8 @@ qmm_gemm_tail_kernel(float *part, int tile0, int mtiles, const GemmOut o, int M,
 // The split tail: when the tiles fill the SMs' last wave poorly (e.g. 320 tiles of
 // 256 x 256 at M = 4096, N = 5120 leave 24 tiles for a third wave of 148 SMs),
 // the full waves run as usual and the remaining tiles are split along K over the
-// SMs (float sums added at L2 into the workspace), then finished by the tail
-// kernel. tail = 0: one launch.
+// SMs (float parts in the workspace), then finished by the tail kernel.
+// tail = 0: one launch.
 struct GemmPlan {
   int mtiles, tiles, full, tail, ksplit;
 };
@@ -330,13 +361,16 @@ GemmPlan plan_gemm(int M, int N, int K) {
   p.full = p.tiles;
   p.tail = 0;
   p.ksplit = 1;
-  if (p.tiles >= sms && rem > 0 && 2 * rem <= sms) {
-    int ks = sms / rem;
+  // the tiles left for a poorly filled last wave (all of them when there are
+  // fewer tiles than SMs)
+  const int left = p.tiles < sms ? p.tiles : rem;
+  if (left > 0 && 2 * left <= sms) {
+    int ks = sms / left;
     if (ks > 16) ks = 16;
     if (ks > steps / 4) ks = steps / 4;
     if (ks >= 3) {  // a 2-way split of a half-empty wave measured slower than none
-      p.full = p.tiles - rem;
-      p.tail = rem;
+      p.full = p.tiles - left;
+      p.tail = left;
       p.ksplit = ks;
     }
   }
@@ -377,39 +411,45 @@ int launch_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const u
     o.yp[0] = y;
   }
   GemmPlan pl = plan_gemm<BN>(M, N, K);
-  // the split tail keeps its sums in the workspace (after the verify path's
-  // count region, whatever the region holds); without one, every tile runs whole
+  // the split tail keeps its parts in the workspace (after the verify path's
+  // count region); without one, every tile runs whole
   float *part = nullptr;
   if (pl.tail) {
-    const size_t need = kGemmPartOffset + (size_t)pl.tail * 256 * BN * sizeof(float);
+    const size_t need = kGemmPartOffset + (size_t)pl.tail * pl.ksplit * 256 * BN * sizeof(float);
     if (ws && ws_bytes >= need && aligned(ws, 256))
       part = reinterpret_cast<float *>(static_cast<unsigned char *>(ws) + kGemmPartOffset);
     else
       pl.full = pl.tiles, pl.tail = 0, pl.ksplit = 1;
   }
-  GemmTiles whole{0, pl.mtiles, 1, part, (long long)pl.tail * 256 * BN};
-  qmm_gemm_kernel<BN><<<pl.full, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, o, whole, M, N, K, ldy);
-  if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
+  GemmTiles whole{0, pl.mtiles, 1, nullptr};
+  if (pl.full) {
+    qmm_gemm_kernel<BN><<<pl.full, C::THREADS, C::SMEM, st>>>(tx, tw, s, b, o, whole, M, N, K, ldy);
+    if (cudaGetLastError() != cudaSuccess) return TSB_ECUDA;
+  }
   if (!pl.tail) return TSB_OK;
-  // the tail starts on SMs as the last full wave's CTAs exit (it touches
-  // nothing the full tiles write)
+  // the split launch starts on SMs as the last full wave's CTAs exit (it
+  // touches nothing the full tiles write); with no full tiles it is the call's
+  // first kernel and waits for the previous work on the stream (x may be its
+  // output). The tail kernel follows it either way.
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pl.full ? 1 : 0;
   cfg.stream = st;
   cfg.gridDim = dim3(pl.tail * pl.ksplit, 1, 1);
   cfg.blockDim = dim3(C::THREADS, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
-  GemmTiles split{pl.full, pl.mtiles, pl.ksplit, part, 0};
+  GemmTiles split{pl.full, pl.mtiles, pl.ksplit, part};
   if (cudaLaunchKernelEx(&cfg, qmm_gemm_kernel<BN>, tx, tw, s, b, o, split, M, N, K, ldy) != cudaSuccess)
     return TSB_ECUDA;
-  cfg.gridDim = dim3(pl.tail * 2, 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(pl.tail * (BN / 8), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
   cfg.dynamicSmemBytes = 0;
-  if (cudaLaunchKernelEx(&cfg, qmm_gemm_tail_kernel<BN>, part, pl.full, pl.mtiles, o, M, ldy) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, qmm_gemm_tail_kernel<BN>, (const float *)part, pl.full, pl.mtiles, pl.ksplit, o, M,
+                         ldy) != cudaSuccess)
     return TSB_ECUDA;
   return TSB_OK;
 }
@@ -427,10 +467,10 @@ int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint
 size_t qmm_gemm_workspace_bytes(int M, int N, int K) {
   if (N % 256 == 0) {
     const GemmPlan p = plan_gemm<256>(M, N, K);
-    return p.tail ? kGemmPartOffset + (size_t)p.tail * 256 * 256 * sizeof(float) : 0;
+    return p.tail ? kGemmPartOffset + (size_t)p.tail * p.ksplit * 256 * 256 * sizeof(float) : 0;
   }
   const GemmPlan p = plan_gemm<128>(M, N, K);
-  return p.tail ? kGemmPartOffset + (size_t)p.tail * 256 * 128 * sizeof(float) : 0;
+  return p.tail ? kGemmPartOffset + (size_t)p.tail * p.ksplit * 256 * 128 * sizeof(float) : 0;
 }
 
 unsigned int status_gemm(bool reset) {
