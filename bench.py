@@ -224,6 +224,27 @@ def run_profile_attn(args):
     print(json.dumps({"profile": "attn", "kv": args.attn_kv, "calls": args.warmup + 1}))
 
 
+def run_profile_prefill(args):
+    """Config-3 prefill (M = 4096, 5120x17408: the shape with a split tail):
+    --warmup calls, then one."""
+    import torch
+
+    import tsb
+    from tsb import ops
+
+    torch.cuda.set_device(0)
+    tsb.load_library()
+    m, n, k = 4096, 5120, 17408
+    torch.manual_seed(3)
+    wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda") * 0.02)
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    for _ in range(args.warmup + 1):
+        ops.quantized_matmul_into(x, wq, s, b, y, n)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": "prefill", "shape": [m, n, k], "calls": args.warmup + 1}))
+
+
 def run_tsb(args):
     import numpy as np
     import torch
@@ -797,9 +818,10 @@ def main():
     ap.add_argument("--impl", choices=["tsb", "reference"], default="tsb")
     ap.add_argument("--no-secondary", dest="secondary", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
-    ap.add_argument("--profile", choices=["qmm", "attn", "decoder"], default=None,
+    ap.add_argument("--profile", choices=["qmm", "attn", "decoder", "prefill"], default=None,
                     help="profiling driver for ncu: --warmup eager steps, then exactly one eager step "
-                         "(qmm: the 15 sweep calls; attn: one config-4 B=1 L=32768 call); no timing")
+                         "(qmm: the 15 sweep calls; attn: one config-4 B=1 L=32768 call; prefill: one "
+                         "M=4096 5120x17408 call); no timing")
     ap.add_argument("--attn-kv", choices=["bf16", "mlx_q8", "ref_q8"], default="bf16",
                     help="KV format of --profile attn")
     args = ap.parse_args()
@@ -811,6 +833,8 @@ def main():
         run_profile_attn(args)
     elif args.profile == "decoder":
         run_profile_decoder(args)
+    elif args.profile == "prefill":
+        run_profile_prefill(args)
     else:
         run_tsb(args)
 
