@@ -64,7 +64,7 @@
 // quantizer-made scales and biases. tsb_dequant_w4g64 follows the reference's
 // two roundings bit for bit. The weights carry the bias, so each group costs
 // only its four K=16 MMAs.
-#include "gather.cuh"
+#include "stream_k.cuh"
 
 #include <string.h>
 
@@ -112,31 +112,6 @@ struct TsCfg {
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
-// Advance a ring position (slot, phase bit) without divisions.
-struct Ring {
-  int slot = 0;
-  uint32_t phase = 0;
-  TSB_HD void next(int n) {
-    if (++slot == n) { slot = 0; phase ^= 1u; }
-  }
-};
-
-// Stream-K partition: CTA c of P owns units [U c / P, U (c+1) / P). The owners
-// of tile t (units [t nst, (t+1) nst)) are CTAs c_lo(t) .. c_hi(t).
-struct Part {
-  long long U;
-  int P, nst;
-  TSB_HD long long start(int c) const { return U * c / P; }
-  TSB_HD int c_lo(int t) const {
-    const long long a = (long long)t * nst;
-    return (int)(((a + 1) * P + U - 1) / U) - 1;
-  }
-  TSB_HD int c_hi(int t) const {
-    const long long b = (long long)(t + 1) * nst;
-    return (int)((b * P + U - 1) / U) - 1;
-  }
-};
-
 struct TsArgs {
   const uint16_t *scales, *biases;
   float *partials;     // [tiles][maxp][NP][128], part 0 unused
@@ -149,22 +124,6 @@ struct TsArgs {
   uint16_t *yp[kMaxGatherRanks];
   uint32_t *sig[kMaxGatherRanks];
 };
-
-TSB_HD uint32_t ld_acquire_gpu(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-TSB_HD void st_release_gpu(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// 16-byte global -> shared copy through L2 (cp.async.cg), completed by cp_async_wait_all.
-TSB_HD void cp_async_cg16(uint32_t dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-TSB_HD void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
 
 template <int NP>
 __global__ void __launch_bounds__(TsCfg<NP>::THREADS, 1)
@@ -628,12 +587,6 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   if (a.world > 1 && threadIdx.x == 0) gather_finish(a.sig, a.world, a.rank, gridDim.x);
 }
 
-// The workspace starts with a fixed flag region for every shape: partials of
-// one call must never land where another shape's call keeps its flags (the
-// region is only ever written with flag stores, so it stays zero between
-// calls), and the partials follow it.
-constexpr size_t kFlagRegionBytes = 64 * 1024;
-
 // Grid and workspace of one call.
 struct TsPlan {
   long long U;
@@ -644,16 +597,13 @@ struct TsPlan {
 template <int NP>
 TsPlan plan_ts(int M, int N, int K) {
   (void)M;
+  const SkPlan sk = plan_stream_k(N, K);
   TsPlan p;
-  p.tiles = N / 128;
-  p.nst = (K / 64 + 3) / 4;
-  p.U = (long long)p.tiles * p.nst;
-  long long P = sm_count();
-  if (P > p.U / 2) P = p.U / 2;  // at least two stages per CTA
-  if (P < 1) P = 1;
-  p.P = (int)P;
-  const long long per = p.U / p.P;  // the shortest range
-  p.maxp = (int)((p.nst + per - 1) / per) + 1;
+  p.U = sk.U;
+  p.P = sk.P;
+  p.nst = sk.nst;
+  p.tiles = sk.tiles;
+  p.maxp = sk.maxp;
   p.flag_bytes = kFlagRegionBytes;  // tiles * maxp flags must fit: checked at launch
   p.part_bytes = (size_t)p.tiles * p.maxp * NP * 128 * sizeof(float);
   return p;
