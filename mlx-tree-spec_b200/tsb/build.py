@@ -14,7 +14,7 @@ ROOT = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(ROOT, "csrc")
 OUT = os.path.join(PKG_DIR, "libtsb.so")
 
-SOURCES = ["api.cu", "dequant_tree.cu", "qmm.cu", "qmm_ts.cu", "qmm_gemm.cu", "attn.cu", "attn_tc.cu", "decoder.cu", "kv_commit.cu", "gdn.cu"]
+SOURCES = ["api.cu", "dequant_tree.cu", "qmm.cu", "qmm_ts.cu", "qmv.cu", "qmm_gemm.cu", "attn.cu", "attn_tc.cu", "decoder.cu", "kv_commit.cu", "gdn.cu"]
 NVCC_FLAGS = [
     "-shared", "-Xcompiler", "-fPIC", "-std=c++17", "-O3", "-lineinfo",
     "-gencode", "arch=compute_100a,code=sm_100a",
