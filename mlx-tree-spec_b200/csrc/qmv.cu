@@ -23,10 +23,11 @@
 // b)), the reference's dequantization rule (qmm_packed.py:200, 348, 635).
 //
 // Work: a persistent grid (one CTA of 16 warps per SM); each warp takes blocks
-// of 4 weight rows (grid-stride), each lane 16 bytes (32 codes, half a group)
-// of each row per step, x read from shared memory once per step for all 4 rows;
-// lanes reduce by shuffles at the end. The first steps' weight loads are issued
-// before waiting for the previous kernel (weights are constant; x is not).
+// of 4 weight rows (grid-stride), each lane 16 bytes (32 codes, half a
+// group) of each row per step, x read from shared memory once per step for the
+// block's rows; lanes reduce by shuffles at the end. The first steps' weight
+// loads are issued before waiting for the previous kernel (weights are
+// constant; x is not).
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -35,7 +36,6 @@ namespace tsb {
 namespace {
 
 constexpr int kQmvWarps = 16;
-constexpr int kQmvRows = 4;           // weight rows per warp block
 constexpr int kQmvMaxSmem = 200 * 1024;
 
 TSB_HD float pow2i(int k) { return __int_as_float((k + 127) << 23); }  // 2^k, k in [-126, 127]
@@ -54,7 +54,9 @@ struct QmvSmem {
   static size_t bytes(int K) { return (size_t)MT * 2 * (K / 8) * 8 + (size_t)MT * (K / 64) * 8; }
 };
 
-template <int MT>
+// RW weight rows per warp block, PF 16-byte chunks of each row in flight per
+// lane (RW * PF = 8: up to 64 KB of weights in flight per SM).
+template <int MT, int RW>
 __global__ void __launch_bounds__(kQmvWarps * 32, 1)
 qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const uint16_t *__restrict__ scales,
            const uint16_t *__restrict__ biases, uint16_t *__restrict__ y, int N, int K, int ldy) {
@@ -63,18 +65,18 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
   uint2 *xp = reinterpret_cast<uint2 *>(smem);                                   // [MT][2][W]
   float2 *gf = reinterpret_cast<float2 *>(smem + (size_t)MT * 2 * W * 8);        // [MT][G]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int nblk = N / kQmvRows;
+  const int nblk = N / RW;
   const int gw = blockIdx.x * kQmvWarps + wid, nw = gridDim.x * kQmvWarps;
 
   if (threadIdx.x == 0) griddep_launch_dependents();
   // the first block's first chunks in flight before x is ready
-  constexpr int PF = 2;  // chunks per row kept in flight
-  uint4 cur[PF][kQmvRows];
+  constexpr int PF = 8 / RW;  // chunks per row kept in flight
+  uint4 cur[PF][RW];
   int blk = gw;
-  auto load_chunks = [&](int b, int v0, uint4 (&dst)[kQmvRows]) {
+  auto load_chunks = [&](int b, int v0, uint4 (&dst)[RW]) {
 #pragma unroll
-    for (int rr = 0; rr < kQmvRows; ++rr)
-      dst[rr] = v0 < V ? ldg_nc_v4(w + ((size_t)(b * kQmvRows + rr) * W) + 4 * (size_t)v0) : make_uint4(0, 0, 0, 0);
+    for (int rr = 0; rr < RW; ++rr)
+      dst[rr] = v0 < V ? ldg_nc_v4(w + ((size_t)(b * RW + rr) * W) + 4 * (size_t)v0) : make_uint4(0, 0, 0, 0);
   };
   if (blk < nblk) {
 #pragma unroll
@@ -82,75 +84,80 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
   }
 
   griddep_wait();  // x may be the previous kernel's output
-  // ---- x -> pieces, one thread per (token, group): 64 elements
-  for (int tg = threadIdx.x; tg < MT * G; tg += blockDim.x) {
+  // ---- x -> pieces: 8 threads per (token, group), one 8-element word each
+  // (MT G 8 is a multiple of 8 and blockDim of 32: a group's threads are 8
+  // consecutive lanes of one warp)
+  for (int base = 0; base < MT * G * 8; base += blockDim.x) {
+    const int i = base + (int)threadIdx.x;
+    const bool ok = i < MT * G * 8;
+    const int tg = i >> 3, wl = i & 7;
     const int t = tg / G, g = tg - t * G;
-    const uint16_t *xg = x + (size_t)t * K + 64 * (size_t)g;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (ok) v = *reinterpret_cast<const uint4 *>(x + (size_t)t * K + 64 * (size_t)g + 8 * wl);
+    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    float fv[8];
     float mx = 0.f, xs = 0.f;
-    bool bad = false;
-    for (int i = 0; i < 64; i += 8) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(xg + i);
-      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+    int bad = 0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float a0 = __uint_as_float(wv[k] << 16), a1 = __uint_as_float(wv[k] & 0xFFFF0000u);
-        xs += a0;
-        xs += a1;
-        const uint32_t m0 = wv[k] & 0x7FFFu, m1 = (wv[k] >> 16) & 0x7FFFu;
-        bad |= (m0 >= 0x7F80u) | (m1 >= 0x7F80u);
-        mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m1 << 16)));
-      }
+    for (int k = 0; k < 4; ++k) {
+      fv[2 * k] = __uint_as_float(wv[k] << 16);
+      fv[2 * k + 1] = __uint_as_float(wv[k] & 0xFFFF0000u);
+      const uint32_t m0 = wv[k] & 0x7FFFu, m1 = (wv[k] >> 16) & 0x7FFFu;
+      bad |= (m0 >= 0x7F80u) | (m1 >= 0x7F80u);
+      mx = fmaxf(mx, fmaxf(__uint_as_float(m0 << 16), __uint_as_float(m1 << 16)));
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) xs += fv[k];
+    // the group's 8 threads: max, any non-finite, and the sum (fixed order)
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+      xs += __shfl_xor_sync(0xffffffffu, xs, o);
+    }
+    if (!ok) continue;
     int e = 0;  // floor(log2(max |x|)), 0 for an all-zero group
     if (mx > 0.f) {
       const uint32_t bits = __float_as_uint(mx);
       const int ex = (int)(bits >> 23);
       e = ex ? ex - 127 : (31 - __clz((int)bits)) - 149;
     }
-    const int a = 5 - e, a1 = a >> 1, a2 = a - a1;   // x c = (x 2^a1) 2^a2
-    const int f = e - 5, f1 = f >> 1, f2 = f - f1;   // 1 / c
+    const int a = 5 - e, a1 = a >> 1, a2 = a - a1;  // x c = (x 2^a1) 2^a2
     const float p1 = pow2i(a1), p2 = pow2i(a2);
-    gf[t * G + g] = make_float2(bad ? __int_as_float(0x7FC00000) : pow2i(f1) * pow2i(f2), xs);
-    for (int i = 0; i < 64; i += 8) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(xg + i);
-      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-      float fv[8];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        fv[2 * k] = __uint_as_float(wv[k] << 16);
-        fv[2 * k + 1] = __uint_as_float(wv[k] & 0xFFFF0000u);
-      }
-      uint32_t q1[2] = {0u, 0u}, q2[2] = {0u, 0u};  // {even codes, odd codes}
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        float tv = (fv[k] * p1) * p2;
-        if (!(fabsf(tv) <= 64.f)) tv = 0.f;  // inf and nan (the group is marked above)
-        const float r1 = rintf(tv);
-        const int i1 = (int)r1, i2 = (int)rintf((tv - r1) * 128.f);
-        q1[k & 1] |= ((uint32_t)i1 & 0xFFu) << (8 * (k >> 1));
-        q2[k & 1] |= ((uint32_t)i2 & 0xFFu) << (8 * (k >> 1));
-      }
-      const int wi = 8 * g + i / 8;
-      xp[(t * 2 + 0) * W + wi] = make_uint2(q1[0], q1[1]);
-      xp[(t * 2 + 1) * W + wi] = make_uint2(q2[0], q2[1]);
+    if (wl == 0) {
+      const int f = e - 5, f1 = f >> 1, f2 = f - f1;  // 1 / c
+      gf[t * G + g] = make_float2(bad ? __int_as_float(0x7FC00000) : pow2i(f1) * pow2i(f2), xs);
     }
+    uint32_t q1[2] = {0u, 0u}, q2[2] = {0u, 0u};  // {even codes, odd codes}
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float tv = (fv[k] * p1) * p2;
+      if (!(fabsf(tv) <= 64.f)) tv = 0.f;  // inf and nan (the group is marked above)
+      const float r1 = rintf(tv);
+      const int i1 = (int)r1, i2 = (int)rintf((tv - r1) * 128.f);
+      q1[k & 1] |= ((uint32_t)i1 & 0xFFu) << (8 * (k >> 1));
+      q2[k & 1] |= ((uint32_t)i2 & 0xFFu) << (8 * (k >> 1));
+    }
+    const int wi = 8 * g + wl;
+    xp[(t * 2 + 0) * W + wi] = make_uint2(q1[0], q1[1]);
+    xp[(t * 2 + 1) * W + wi] = make_uint2(q2[0], q2[1]);
   }
   __syncthreads();
 
-  // ---- rows: 4 per warp block, 16 bytes of each row per lane and step
+  // ---- rows: RW per warp block, 16 bytes of each row per lane and step
   for (; blk < nblk; blk += nw) {
-    float acc[kQmvRows][MT];
+    float acc[RW][MT];
 #pragma unroll
-    for (int rr = 0; rr < kQmvRows; ++rr)
+    for (int rr = 0; rr < RW; ++rr)
 #pragma unroll
       for (int t = 0; t < MT; ++t) acc[rr][t] = 0.f;
     for (int v0 = lane; v0 < V; v0 += 32 * PF) {
 #pragma unroll
       for (int i = 0; i < PF; ++i) {
         const int v = v0 + 32 * i;
-        uint4 c[kQmvRows];
+        uint4 c[RW];
 #pragma unroll
-        for (int rr = 0; rr < kQmvRows; ++rr) c[rr] = cur[i][rr];
+        for (int rr = 0; rr < RW; ++rr) c[rr] = cur[i][rr];
         // the chunk PF steps ahead (or the next block's first ones)
         int nb = blk, nv = v + 32 * PF;
         if (nv >= V) { nb = blk + nw; nv = lane + 32 * i; }
@@ -171,8 +178,8 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
 #pragma unroll
         for (int t = 0; t < MT; ++t) gv[t] = gf[t * G + g];
 #pragma unroll
-        for (int rr = 0; rr < kQmvRows; ++rr) {
-          const int row = blk * kQmvRows + rr;
+        for (int rr = 0; rr < RW; ++rr) {
+          const int row = blk * RW + rr;
           const float s = bf16_bits_to_float(__ldg(scales + (size_t)row * G + g));
           const uint32_t cw[4] = {c[rr].x, c[rr].y, c[rr].z, c[rr].w};
           uint32_t lo[4], hi[4];
@@ -205,20 +212,20 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
     }
     // lanes -> row sums (fixed order), lane rr * MT + t writes
 #pragma unroll
-    for (int rr = 0; rr < kQmvRows; ++rr)
+    for (int rr = 0; rr < RW; ++rr)
 #pragma unroll
       for (int t = 0; t < MT; ++t)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc[rr][t] += __shfl_xor_sync(0xffffffffu, acc[rr][t], o);
 #pragma unroll
-    for (int rr = 0; rr < kQmvRows; ++rr)
+    for (int rr = 0; rr < RW; ++rr)
 #pragma unroll
       for (int t = 0; t < MT; ++t)
-        if (lane == rr * MT + t) y[(size_t)t * ldy + blk * kQmvRows + rr] = float_to_bf16_bits(acc[rr][t]);
+        if (lane == rr * MT + t) y[(size_t)t * ldy + blk * RW + rr] = float_to_bf16_bits(acc[rr][t]);
   }
 }
 
-template <int MT>
+template <int MT, int RW>
 int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int N, int K,
                int ldy, cudaStream_t st) {
   const size_t smem = QmvSmem<MT>::bytes(K);
@@ -227,13 +234,13 @@ int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const ui
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    if (cudaFuncSetAttribute(qmv_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kQmvMaxSmem) !=
+    if (cudaFuncSetAttribute(qmv_kernel<MT, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kQmvMaxSmem) !=
         cudaSuccess)
       return TSB_ECUDA;
     attr_dev = dev;
   }
   int blocks = sm_count();
-  const int nblk = N / kQmvRows;
+  const int nblk = N / RW;
   const int need = (nblk + kQmvWarps - 1) / kQmvWarps;
   if (need < blocks) blocks = need;
   cudaLaunchConfig_t cfg = {};
@@ -246,7 +253,7 @@ int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const ui
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<MT>, x, w, s, b, y, N, K, ldy);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<MT, RW>, x, w, s, b, y, N, K, ldy);
   return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
@@ -255,8 +262,10 @@ int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const ui
 // M in {1, 2}, N % 4 == 0, K % 64 == 0 (callers check N % 128 and alignment).
 int qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N, int K,
         int ldy, cudaStream_t st) {
-  if (M == 1) return launch_qmv<1>(x, w, s, b, y, N, K, ldy, st);
-  if (M == 2) return launch_qmv<2>(x, w, s, b, y, N, K, ldy, st);
+  // 4-row warp blocks: 2-row blocks (more warps streaming when N / 4 is below
+  // the device's warp count) measured slower on B200 (5120x17408: 19.7 -> 28.2 us)
+  if (M == 1) return launch_qmv<1, 4>(x, w, s, b, y, N, K, ldy, st);
+  if (M == 2) return launch_qmv<2, 4>(x, w, s, b, y, N, K, ldy, st);
   return TSB_EINVAL;
 }
 
