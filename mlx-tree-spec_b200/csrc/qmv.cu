@@ -66,7 +66,10 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
   float2 *gf = reinterpret_cast<float2 *>(smem + (size_t)MT * 2 * W * 8);        // [MT][G]
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nblk = N / RW;
-  const int gw = blockIdx.x * kQmvWarps + wid, nw = gridDim.x * kQmvWarps;
+  // warp w of CTA c takes the blocks w * gridDim + c + k * nw: consecutive
+  // blocks go to different CTAs, so every SM streams even when there are fewer
+  // blocks than warps
+  const int gw = wid * gridDim.x + blockIdx.x, nw = gridDim.x * kQmvWarps;
 
   if (threadIdx.x == 0) griddep_launch_dependents();
   // the first block's first chunks in flight before x is ready
@@ -241,8 +244,7 @@ int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const ui
   }
   int blocks = sm_count();
   const int nblk = N / RW;
-  const int need = (nblk + kQmvWarps - 1) / kQmvWarps;
-  if (need < blocks) blocks = need;
+  if (nblk < blocks) blocks = nblk;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(blocks, 1, 1);
   cfg.blockDim = dim3(kQmvWarps * 32, 1, 1);
