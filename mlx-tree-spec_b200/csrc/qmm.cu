@@ -11,10 +11,10 @@ int qmm_gemm(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint
              int K, int ldy, const GatherSpec *gs, void *ws, size_t ws_bytes, cudaStream_t st);
 size_t qmm_gemm_workspace_bytes(int M, int N, int K);
 int qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N, int K,
-        int ldy, cudaStream_t st);
+        int ldy, const GatherSpec *gs, cudaStream_t st);
 
-// Rows up to which the CUDA-core GEMV (qmv.cu) takes the single-GPU call: it
-// has no per-call pipeline to fill, which at M <= 2 costs more than it saves.
+// Rows up to which the CUDA-core GEMV (qmv.cu) takes the call: it has no
+// per-call pipeline to fill, which at M <= 2 costs more than it saves.
 constexpr int kQmvMaxRows = 2;
 
 // Rows above which the tcgen05 GEMM (dequantize into shared memory, 256-row
@@ -42,7 +42,7 @@ extern "C" int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scale
   if (!aligned(x, 16) || !aligned(w, 16) || !aligned(y, 16)) return TSB_EINVAL;
   if (M <= kQmvMaxRows) {
     const int r = qmv((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, (uint16_t *)y, M, N,
-                      K, ldy, (cudaStream_t)stream);
+                      K, ldy, nullptr, (cudaStream_t)stream);
     if (r != TSB_EUNSUPPORTED) return r;  // else (x too long for shared memory) the verify kernel
   }
   if (M <= kTsMaxRows)
@@ -78,6 +78,11 @@ extern "C" int tsb_qmm_w4g64_gather(const void *x, const uint32_t *w, const void
     gs.sig[p] = g->sig[p];
   }
   uint16_t *y_own = (uint16_t *)g->y[g->rank] + gs.col0;
+  if (M <= kQmvMaxRows) {
+    const int r = qmv((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, y_own, M, Ns, K,
+                      ldy, &gs, (cudaStream_t)stream);
+    if (r != TSB_EUNSUPPORTED) return r;
+  }
   if (M <= kTsMaxRows)
     return qmm_ts((const uint16_t *)x, w, (const uint16_t *)scales, (const uint16_t *)biases, y_own, M, Ns, K, ldy,
                   ws, ws_bytes, &gs, (cudaStream_t)stream);

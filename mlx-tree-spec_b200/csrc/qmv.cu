@@ -28,14 +28,22 @@
 // block's rows; lanes reduce by shuffles at the end. The first steps' weight
 // loads are issued before waiting for the previous kernel (weights are
 // constant; x is not).
-#include "common.cuh"
-#include "sm100.cuh"
+#include "gather.cuh"
 
 namespace tsb {
 
 namespace {
 
 constexpr int kQmvWarps = 16;
+
+// Where the outputs go: yp[p] is rank p's y at this rank's first column (world
+// 1: yp[0] is y); sig[p] is rank p's signal block (the handshakes of
+// gather.cuh, as in the tcgen05 kernels).
+struct QmvOut {
+  int world, rank;
+  uint16_t *yp[kMaxGatherRanks];
+  uint32_t *sig[kMaxGatherRanks];
+};
 constexpr int kQmvMaxSmem = 200 * 1024;
 
 TSB_HD float pow2i(int k) { return __int_as_float((k + 127) << 23); }  // 2^k, k in [-126, 127]
@@ -59,7 +67,7 @@ struct QmvSmem {
 template <int MT, int RW>
 __global__ void __launch_bounds__(kQmvWarps * 32, 1)
 qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const uint16_t *__restrict__ scales,
-           const uint16_t *__restrict__ biases, uint16_t *__restrict__ y, int N, int K, int ldy) {
+           const uint16_t *__restrict__ biases, const QmvOut o, int N, int K, int ldy) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int W = K / 8, G = K / 64, V = K / 32;  // words, groups, 16-byte chunks per row
   uint2 *xp = reinterpret_cast<uint2 *>(smem);                                   // [MT][2][W]
@@ -87,6 +95,11 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
   }
 
   griddep_wait();  // x may be the previous kernel's output
+  // Gather over GPUs: this call's epoch (the previous call has completed). CTA 0
+  // tells every peer that this rank has started it; stores into a peer's y
+  // wait (below, once per CTA) until that peer has started it too.
+  const uint32_t ep = o.world > 1 ? gather_epoch(o.sig, o.world, o.rank) : 0u;
+  if (o.world > 1 && blockIdx.x == 0 && threadIdx.x == 0) gather_start(o.sig, o.world, o.rank, ep);
   // ---- x -> pieces: 8 threads per (token, group), one 8-element word each
   // (MT G 8 is a multiple of 8 and blockDim of 32: a group's threads are 8
   // consecutive lanes of one warp)
@@ -145,6 +158,7 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
     xp[(t * 2 + 0) * W + wi] = make_uint2(q1[0], q1[1]);
     xp[(t * 2 + 1) * W + wi] = make_uint2(q2[0], q2[1]);
   }
+  if (o.world > 1 && threadIdx.x == 0) wait_peers(o.sig[o.rank], o.world, o.rank, ep);
   __syncthreads();
 
   // ---- rows: RW per warp block, 16 bytes of each row per lane and step
@@ -224,13 +238,21 @@ qmv_kernel(const uint16_t *__restrict__ x, const uint32_t *__restrict__ w, const
     for (int rr = 0; rr < RW; ++rr)
 #pragma unroll
       for (int t = 0; t < MT; ++t)
-        if (lane == rr * MT + t) y[(size_t)t * ldy + blk * RW + rr] = float_to_bf16_bits(acc[rr][t]);
+        if (lane == rr * MT + t) {
+          const uint16_t v = float_to_bf16_bits(acc[rr][t]);
+          for (int p = 0; p < o.world; ++p) o.yp[p][(size_t)t * ldy + blk * RW + rr] = v;
+        }
+  }
+  if (o.world > 1) {
+    // every store of this CTA precedes the finish handshake's release
+    __syncthreads();
+    if (threadIdx.x == 0) gather_finish(o.sig, o.world, o.rank, gridDim.x);
   }
 }
 
 template <int MT, int RW>
-int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int N, int K,
-               int ldy, cudaStream_t st) {
+int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, const QmvOut &o, int N,
+               int K, int ldy, cudaStream_t st) {
   const size_t smem = QmvSmem<MT>::bytes(K);
   if (smem > (size_t)kQmvMaxSmem) return TSB_EUNSUPPORTED;
   static int attr_dev = -1;
@@ -255,19 +277,35 @@ int launch_qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const ui
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<MT, RW>, x, w, s, b, y, N, K, ldy);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmv_kernel<MT, RW>, x, w, s, b, o, N, K, ldy);
   return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 }  // namespace
 
 // M in {1, 2}, N % 4 == 0, K % 64 == 0 (callers check N % 128 and alignment).
+// gs: the tensor-parallel form (this rank's N-shard, stored into every rank's
+// y), else y alone.
 int qmv(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N, int K,
-        int ldy, cudaStream_t st) {
+        int ldy, const GatherSpec *gs, cudaStream_t st) {
+  QmvOut o;
+  for (int p = 0; p < kMaxGatherRanks; ++p) { o.yp[p] = nullptr; o.sig[p] = nullptr; }
+  if (gs) {
+    o.world = gs->world;
+    o.rank = gs->rank;
+    for (int p = 0; p < gs->world; ++p) {
+      o.yp[p] = static_cast<uint16_t *>(gs->y[p]) + gs->col0;
+      o.sig[p] = static_cast<uint32_t *>(gs->sig[p]);
+    }
+  } else {
+    o.world = 1;
+    o.rank = 0;
+    o.yp[0] = y;
+  }
   // 4-row warp blocks: 2-row blocks (more warps streaming when N / 4 is below
   // the device's warp count) measured slower on B200 (5120x17408: 19.7 -> 28.2 us)
-  if (M == 1) return launch_qmv<1, 4>(x, w, s, b, y, N, K, ldy, st);
-  if (M == 2) return launch_qmv<2, 4>(x, w, s, b, y, N, K, ldy, st);
+  if (M == 1) return launch_qmv<1, 4>(x, w, s, b, o, N, K, ldy, st);
+  if (M == 2) return launch_qmv<2, 4>(x, w, s, b, o, N, K, ldy, st);
   return TSB_EINVAL;
 }
 

@@ -4,7 +4,7 @@ GEMM): each rank's output holds every rank's columns, bit-identical to each
 shard's single-GPU result, across repeated calls into the same buffer, eager
 and replayed from a CUDA graph. The prefill (M = 4096) with NCCL all-gathers
 overlapped against the row blocks' matmuls (ShardedQMM chunks): bit-identical
-likewise.
+to the single-GPU results of the same row blocks.
 
 Each world size needs that many GPUs (skipped otherwise): ranks that wait on
 one another never share a GPU."""
@@ -78,8 +78,12 @@ def _worker(rank, world, port, q):
             wq, s, b = tsb.quantize(torch.randn(n, k, device="cuda", generator=g) * 0.02)
             x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
             shards = [tdist.shard_weight(wq, s, b, world, r) for r in range(world)]
-            ref = torch.cat([ops.quantized_matmul(x, *sh) for sh in shards], dim=1)
             for chunks in (1, 4):
+                # each row block is one single-GPU call of M / chunks rows (the
+                # prefill GEMM's split of its last wave depends on M)
+                c = m // chunks
+                ref = torch.cat([torch.cat([ops.quantized_matmul(x[i * c:(i + 1) * c], *sh) for sh in shards], dim=1)
+                                 for i in range(chunks)], dim=0)
                 out = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
                 sq.forward_into(x, *shards[rank], out, chunks=chunks)
                 torch.cuda.synchronize()
