@@ -152,6 +152,30 @@ int tsb_dequant_w4g64(const uint32_t *w, const void *scales, const void *biases,
 int tsb_tree_ancestor_bits(const int32_t *parents, int B, int T, uint64_t *bits, int32_t *depth,
                            tsb_stream_t stream);
 
+/* Element types of an attention mask read by tsb_tree_mask_bits. */
+enum {
+  TSB_MASK_BOOL = 0, /* uint8: nonzero = visible                                  */
+  TSB_MASK_BF16 = 1, /* additive bf16: +-0 = visible, -inf = hidden               */
+  TSB_MASK_F16 = 2,  /* additive fp16: +-0 = visible, -inf = hidden               */
+  TSB_MASK_F32 = 3   /* additive float: +-0 = visible, -inf = hidden              */
+};
+
+/* An attention mask in the form SDPA takes -> the bit form tsb_tree_attn
+ * takes: the inverse of Tree.mask (mlx-tree-spec src/mlx_tree_spec/
+ * tree_verify.py:131-139, where(anc, 0, -inf) after `offset` zero columns),
+ * for callers that hold the reference's additive mask (the mlx-lm SDPA hook,
+ * long_attention.py:69-88; the SDPA fallback, tree_verify.py:363-366).
+ *
+ *   mask  rows x L elements of mask_dtype, row r at element r * row_stride
+ *   bits  uint64 [rows]: bit j set iff column L - tail + j is visible
+ *   bad   int32 [1], set to the number of rows the bit form cannot express:
+ *         a hidden column before the last `tail`, or an additive value that
+ *         is neither +-0 nor -inf (a bias, +inf, NaN). Such a row's bits are
+ *         meaningless; the caller keeps the mask (its own SDPA).
+ * Requirements: rows >= 1, 0 <= tail <= L <= row_stride, tail <= 64. */
+int tsb_tree_mask_bits(const void *mask, int mask_dtype, int rows, long long L, long long row_stride, int tail,
+                       uint64_t *bits, int32_t *bad, tsb_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Tree-mask flash attention (split-KV flash decoding with fused combine).
  *

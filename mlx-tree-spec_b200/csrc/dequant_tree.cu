@@ -6,6 +6,8 @@
 // bf16_rne(fmaf(q, s, b)).
 // tsb_tree_ancestor_bits follows Tree.__init__ (tree_verify.py:66-121) and
 // ancestor_bits (tree_flash.py:146-148), extended to forests.
+// tsb_tree_mask_bits inverts Tree.mask (tree_verify.py:131-139): an SDPA mask
+// whose columns before the tree rows are all visible becomes per-row bits.
 #include "common.cuh"
 
 namespace tsb {
@@ -69,6 +71,58 @@ __global__ void ancestor_bits_kernel(const int32_t *__restrict__ parents, int B,
   if (depth) depth[idx] = ok ? d : -1;
 }
 
+// Visibility of mask element c of a row: 1 visible, 0 hidden, -1 neither
+// (an additive value other than +-0 and -inf).
+__device__ __forceinline__ int mask_class(const unsigned char *row, int dt, long long c) {
+  switch (dt) {
+    case TSB_MASK_BOOL:
+      return row[c] != 0;
+    case TSB_MASK_BF16:
+    case TSB_MASK_F16: {
+      const uint16_t v = reinterpret_cast<const uint16_t *>(row)[c];
+      if ((v & 0x7FFFu) == 0) return 1;
+      return v == (dt == TSB_MASK_BF16 ? 0xFF80u : 0xFC00u) ? 0 : -1;
+    }
+    default: {
+      const uint32_t v = reinterpret_cast<const uint32_t *>(row)[c];
+      if ((v & 0x7FFFFFFFu) == 0) return 1;
+      return v == 0xFF800000u ? 0 : -1;
+    }
+  }
+}
+
+// One CTA per mask row, threads striding over the columns (coalesced): the
+// columns before the last `tail` must be visible, the tail columns give the
+// row's bits. `bad` was zeroed on the stream before the launch.
+__global__ void __launch_bounds__(256) mask_bits_kernel(const unsigned char *__restrict__ mask, int dt, int esize,
+                                                        long long L, long long row_stride, int tail,
+                                                        unsigned long long *__restrict__ bits,
+                                                        int32_t *__restrict__ bad) {
+  __shared__ unsigned long long s_bits;
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) {
+    s_bits = 0ull;
+    s_bad = 0;
+  }
+  __syncthreads();
+  const unsigned char *row = mask + (size_t)blockIdx.x * (size_t)row_stride * esize;
+  const long long lo = L - tail;
+  unsigned long long m = 0ull;
+  int b = 0;
+  for (long long c = threadIdx.x; c < L; c += blockDim.x) {
+    const int k = mask_class(row, dt, c);
+    if (k < 0 || (k == 0 && c < lo)) b = 1;
+    else if (k == 1 && c >= lo) m |= 1ull << (c - lo);
+  }
+  if (m) atomicOr(&s_bits, m);
+  if (b) atomicOr(&s_bad, 1);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    bits[blockIdx.x] = s_bits;
+    if (s_bad) atomicAdd(bad, 1);
+  }
+}
+
 }  // namespace tsb
 
 using namespace tsb;
@@ -96,5 +150,26 @@ extern "C" int tsb_tree_ancestor_bits(const int32_t *parents, int B, int T, uint
   const int n = B * T;
   ancestor_bits_kernel<<<(n + 127) / 128, 128, 0, (cudaStream_t)stream>>>(parents, B, T,
                                                                           (unsigned long long *)bits, depth);
+  return launch_status();
+}
+
+extern "C" int tsb_tree_mask_bits(const void *mask, int mask_dtype, int rows, long long L, long long row_stride,
+                                  int tail, uint64_t *bits, int32_t *bad, tsb_stream_t stream) {
+  if (!mask || !bits || !bad) return TSB_EINVAL;
+  int esize = 0;
+  switch (mask_dtype) {
+    case TSB_MASK_BOOL: esize = 1; break;
+    case TSB_MASK_BF16:
+    case TSB_MASK_F16: esize = 2; break;
+    case TSB_MASK_F32: esize = 4; break;
+    default: return TSB_EINVAL;
+  }
+  if (rows <= 0 || L <= 0 || row_stride < L || tail < 0 || tail > L) return TSB_EINVAL;
+  if (!aligned(mask, esize)) return TSB_EINVAL;
+  if (tail > 64) return TSB_EUNSUPPORTED;
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(bad, 0, sizeof(int32_t), st) != cudaSuccess) return TSB_ECUDA;
+  mask_bits_kernel<<<rows, 256, 0, st>>>(static_cast<const unsigned char *>(mask), mask_dtype, esize, L, row_stride,
+                                         tail, (unsigned long long *)bits, bad);
   return launch_status();
 }

@@ -1,7 +1,7 @@
 """tsb: the B200-native verify-pass hot path of mlx-tree-spec.
 
 Operators (reference-facing, over torch CUDA tensors):
-  quantized_matmul, dequantize, ancestor_bits, tree_flash
+  quantized_matmul, dequantize, ancestor_bits, tree_flash, mask_bits, sdpa
 Containers: KVCache, Q8KVCache, MLXQ8KVCache
 Input makers: quantize, quantize_rows, quantize_g64
 Sharding: tsb.dist (N-sharded qmm: GatheredQMM gathers the output inside the
@@ -22,7 +22,8 @@ from . import _lib
 from ._lib import (TSB_KV_BF16, TSB_KV_MLX_Q8_G64, TSB_KV_REF_Q8_ROW, TSBError,  # noqa: F401
                    load as load_library)
 from .cache import KVCache, MLXQ8KVCache, Q8KVCache  # noqa: F401
-from .ops import ancestor_bits, commit, dequantize, keep_kv, quantized_matmul, tree_flash, workspace  # noqa: F401
+from .ops import (ancestor_bits, commit, dequantize, keep_kv, mask_bits, quantized_matmul, sdpa,  # noqa: F401
+                  tree_flash, workspace)
 from .quant import quantize, quantize_g64, quantize_rows  # noqa: F401
 
 __version__ = "0.1.0"

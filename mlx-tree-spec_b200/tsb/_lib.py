@@ -24,6 +24,11 @@ TSB_KV_BF16 = 0
 TSB_KV_MLX_Q8_G64 = 1
 TSB_KV_REF_Q8_ROW = 2
 
+TSB_MASK_BOOL = 0
+TSB_MASK_BF16 = 1
+TSB_MASK_F16 = 2
+TSB_MASK_F32 = 3
+
 TSB_MAX_GATHER_RANKS = 8
 
 
@@ -36,7 +41,7 @@ class GatherT(ctypes.Structure):
 
 
 # Every symbol include/tsb.h declares, with (restype, argtypes).
-_P, _I, _Z, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_float
+_P, _I, _Z, _F, _LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_float, ctypes.c_longlong
 SIGNATURES = {
     "tsb_strerror": (ctypes.c_char_p, [_I]),
     "tsb_version": (_I, []),
@@ -46,6 +51,7 @@ SIGNATURES = {
     "tsb_qmm_w4g64_gather": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(GatherT), _P, _Z, _P]),
     "tsb_dequant_w4g64": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "tsb_tree_ancestor_bits": (_I, [_P, _I, _I, _P, _P, _P]),
+    "tsb_tree_mask_bits": (_I, [_P, _I, _I, _LL, _LL, _I, _P, _P, _P]),
     "tsb_tree_attn_workspace_bytes": (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     "tsb_tree_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _F,
                            _P, _P, _P, _Z, _P]),

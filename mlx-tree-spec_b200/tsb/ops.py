@@ -14,6 +14,11 @@ same argument names and meaning:
   tree_flash(queries, cache, scale, bits, tail=None, stats=False)
       = tree_flash.tree_flash (tree_flash.py:151-196); also takes `parents=`
         so the mask is built inside the kernel.
+  mask_bits(mask, tail)
+      = the inverse of Tree.mask (tree_verify.py:131-139): an SDPA mask -> bits
+  sdpa(queries, keys, values, cache, scale, mask, fallback=None)
+      = the mlx-lm SDPA hook of long_attention.install (long_attention.py:
+        69-88) with kv8.attention's routing (kv8.py:162-188)
   keep_kv(cache, off0, nodes) / commit(caches, off0, nodes)
       = tree_verify._keep_kv / the attention-cache part of tree_verify.commit
         (tree_verify.py:487-516): keep the accepted path's K/V rows.
@@ -31,7 +36,8 @@ import ctypes
 import torch
 
 from . import _lib
-from ._lib import TSB_EUNSUPPORTED, TSB_KV_BF16, TSB_KV_MLX_Q8_G64, TSB_KV_REF_Q8_ROW, check
+from ._lib import (TSB_EUNSUPPORTED, TSB_KV_BF16, TSB_KV_MLX_Q8_G64, TSB_KV_REF_Q8_ROW, TSB_MASK_BF16,
+                   TSB_MASK_BOOL, TSB_MASK_F16, TSB_MASK_F32, check)
 
 _WS: dict[int, torch.Tensor] = {}
 
@@ -159,6 +165,38 @@ def ancestor_bits(parents, depth: bool = False):
     return (bits, dep) if depth else bits
 
 
+_MASK_TYPES = {torch.bool: TSB_MASK_BOOL, torch.uint8: TSB_MASK_BOOL, torch.bfloat16: TSB_MASK_BF16,
+               torch.float16: TSB_MASK_F16, torch.float32: TSB_MASK_F32}
+
+
+def mask_bits(mask, tail: int):
+    """An SDPA mask on the GPU -> (bits, bad): the inverse of Tree.mask
+    (tree_verify.py:131-139). mask (..., L): boolean (True visible) or additive
+    (0 visible, -inf hidden) in bf16 / fp16 / float32. bits int64 (...,): bit
+    j set iff column L - tail + j is visible. bad: int32 (1,) on the device,
+    the number of rows the bit form cannot express (a hidden column before the
+    last `tail`, or an additive value other than 0 and -inf); read it before
+    trusting bits. None if the mask type or tail (> 64) is not taken."""
+    _require_cuda(mask)
+    dt = _MASK_TYPES.get(mask.dtype)
+    if dt is None or mask.dim() < 1 or not 0 <= tail <= min(64, mask.shape[-1]):
+        return None
+    L = mask.shape[-1]
+    lead = tuple(mask.shape[:-1])
+    m2 = mask.reshape(-1, L)
+    if m2.stride(-1) != 1 or (m2.shape[0] > 1 and m2.stride(0) < L):
+        m2 = m2.contiguous()
+    rows = m2.shape[0]
+    row_stride = m2.stride(0) if rows > 1 else L
+    bits = torch.empty(rows, dtype=torch.int64, device=mask.device)
+    bad = torch.empty(1, dtype=torch.int32, device=mask.device)
+    lib = _lib.load()
+    st = lib.tsb_tree_mask_bits(_ptr(m2), dt, rows, L, row_stride, tail, _ptr(bits), _ptr(bad), _stream(m2))
+    if check(st, "tsb_tree_mask_bits") == TSB_EUNSUPPORTED:
+        return None
+    return bits.reshape(lead), bad
+
+
 def _kv_planes(cache):
     """(format, k, k_scales, k_biases, v, v_scales, v_biases) of a cache object."""
     fmt = getattr(cache, "kv_format", None)
@@ -223,6 +261,78 @@ def tree_flash(queries, cache, scale: float, bits=None, tail: int | None = None,
         return None
     if stats:
         return out, lse[..., None], torch.ones_like(lse)[..., None]
+    return out
+
+
+class _Rows:
+    """Keys and values with no cache object around them: every row is a key."""
+
+    def __init__(self, keys, values):
+        self.keys, self.values, self.offset = keys, values, keys.shape[2]
+
+
+def _causal_bits(n: int, device) -> torch.Tensor:
+    """Tail-causal masks: node q sees tail rows 0..q (kv8.py:194-197 causal_bits)."""
+    return torch.tensor([(1 << (q + 1)) - 1 if q < 63 else -1 for q in range(n)], dtype=torch.int64, device=device)
+
+
+def _sdpa_tree(queries, keys, values, cache, scale, mask):
+    n = queries.shape[2]
+    if n > 64:
+        return None
+    src = cache if cache is not None and getattr(cache, "keys", None) is not None else _Rows(keys, values)
+    if mask is None or (isinstance(mask, str) and mask == "causal"):
+        bits = _causal_bits(n, queries.device)
+    elif not isinstance(mask, torch.Tensor):
+        return None
+    else:
+        m = mask
+        if m.dim() < 2 or m.shape[-2] != n or m.shape[-1] != int(src.offset):
+            return None
+        if m.dim() == 4:  # (B, heads, n, L): one mask for every head only
+            if m.shape[1] != 1:
+                return None
+            m = m[:, 0]
+        if m.dim() == 3:  # (B, n, L)
+            if m.shape[0] == 1:
+                m = m[0]
+            elif m.shape[0] != queries.shape[0]:
+                return None
+        if m.dim() not in (2, 3):
+            return None
+        r = mask_bits(m, n)
+        if r is None:
+            return None
+        bits, bad = r
+        if int(bad.item()) != 0:
+            return None
+    return tree_flash(queries, src, scale, bits, tail=n)
+
+
+def sdpa(queries, keys, values, cache, scale, mask, *args, fallback=None, **kwargs):
+    """The mlx-lm scaled_dot_product_attention hook (long_attention.py:69-88,
+    install().sdpa) over tsb's tree attention, with kv8.attention's routing of
+    the 8-bit caches (kv8.py:162-188) and batch_attention's SDPA fallback
+    (tree_verify.py:359-366).
+
+    queries (B, Hq, n, D) bf16. cache: a KVCache / Q8KVCache / MLXQ8KVCache
+    whose first `offset` rows are the keys, the queries' own rows last; with
+    cache None, keys and values (B, Hkv, L, D) bf16 are all keys. mask: None
+    or "causal" (the reference's tail-causal rule on this path: query i sees
+    the rows before the last n and tail rows 0..i), or a boolean / additive
+    (0 or -inf) tensor whose last two dims are (n, keys) and whose leading
+    dims are 1 or the batch over requests and 1 over heads, such as
+    Tree.mask (tree_verify.py:131-139). A tensor mask is converted by
+    tsb_tree_mask_bits, which costs one device->host read of its status.
+
+    Returns out (B, Hq, n, D) bf16. What the kernel does not take (a mask that
+    is not a visibility mask, n > 64, extra arguments, a shape the kernel
+    declines) goes to fallback(queries, keys, values, cache=cache,
+    scale=scale, mask=mask, *args, **kwargs) -- the hooked original, as the
+    reference's hook does -- or returns None with no fallback."""
+    out = None if args or kwargs else _sdpa_tree(queries, keys, values, cache, scale, mask)
+    if out is None and fallback is not None:
+        return fallback(queries, keys, values, *args, cache=cache, scale=scale, mask=mask, **kwargs)
     return out
 
 

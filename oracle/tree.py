@@ -82,3 +82,27 @@ def additive_mask(parents, offset: int) -> np.ndarray:
     m[:, :offset] = 0
     m[:, offset:][anc] = 0
     return m
+
+
+def mask_bits(mask, tail: int):
+    """The inverse of additive_mask / Tree.mask (tree_verify.py:131-139), as
+    the build's tsb_tree_mask_bits states it. mask [rows, L]: boolean (True
+    visible) or additive float (0 visible, -inf hidden). Returns (bits uint64
+    [rows]: bit j set iff column L - tail + j is visible, bad bool [rows]: a
+    hidden column before the last `tail`, or an additive value other than 0
+    and -inf)."""
+    m = np.asarray(mask)
+    rows, L = m.shape
+    if m.dtype == bool or m.dtype == np.uint8:
+        vis = m != 0
+        other = np.zeros_like(vis)
+    else:
+        f = m.astype(np.float64)
+        vis = f == 0
+        other = ~vis & ~(np.isneginf(f))
+    lo = L - tail
+    bad = other.any(axis=1) | (~vis[:, :lo]).any(axis=1)
+    bits = np.zeros(rows, dtype=np.uint64)
+    for r in range(rows):
+        bits[r] = np.uint64(sum(1 << j for j in range(tail) if vis[r, lo + j]))
+    return bits, bad

@@ -164,6 +164,26 @@ def test_visibility_equals_additive_mask():
     assert np.array_equal(vis, tree.additive_mask(p, off) == 0)
 
 
+
+def test_mask_bits_inverts_additive_mask():
+    """Tree.mask (tree_verify.py:131-139) read back as bits gives the tree's
+    ancestor bits; the boolean form the same; a bias value or a hidden prefix
+    column is flagged."""
+    rng = np.random.default_rng(11)
+    for t, off in [(1, 0), (5, 3), (17, 40), (64, 9)]:
+        p = gen.tree_parents(rng, t)
+        m = tree.additive_mask(p, off)
+        bits, bad = tree.mask_bits(m, t)
+        assert np.array_equal(bits, tree.ancestor_bits_u64(p)) and not bad.any()
+        bits_b, bad_b = tree.mask_bits(m == 0, t)
+        assert np.array_equal(bits_b, bits) and not bad_b.any()
+    m = tree.additive_mask([-1, 0, 1], 4)
+    m[1, 5] = -1.0  # a bias inside the tree rows
+    m[2, 0] = -np.inf  # a hidden prefix column
+    bits, bad = tree.mask_bits(m, 3)
+    assert list(bad) == [False, True, True]
+    assert int(bits[0]) == 1
+
 def test_golden_ancestors_regenerate():
     g = load_golden("ancestors.npz")
     for key in [k[: -len("_parents")] for k in g if k.endswith("_parents")]:
