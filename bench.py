@@ -41,6 +41,8 @@ for _p in (ROOT, PKG):
 SHAPES = ((6144, 5120), (34816, 5120), (5120, 17408))
 SWEEP_M = (1, 8, 16, 32, 64)
 METRIC = "4-bit qmm HBM TB/s (M<=64 verify sweep)"
+WORKLOAD = ("verify-pass qmm sweep: M in {1,8,16,32,64} x (N,K) in "
+            "{(6144,5120),(34816,5120),(5120,17408)}, 4-bit g64 MLX format")
 UNIT = "TB/s"
 
 
@@ -420,8 +422,7 @@ def run_tsb(args):
             "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "verify-pass qmm sweep: M in {1,8,16,32,64} x (N,K) in "
-                                   "{(6144,5120),(34816,5120),(5120,17408)}, 4-bit g64 MLX format",
+            "config": {"workload": WORKLOAD,
                        "bytes_per_step": total_bytes, "calls_per_step": len(calls),
                        "l2": "inputs larger than L2: rotating weight pool, >= 2.5 x 126 MiB of distinct copies per shape",
                        "parallelism": (f"N-shard x{world}, output gathered inside the qmm kernel (peer stores "
@@ -741,70 +742,89 @@ def cpu_model() -> str:
     return "unknown"
 
 
-def cpu_baseline_sample():
-    """The oracle port on this host's cores: the 3 shapes at M=16 (one call each)."""
+def _cpu_sweep_data(rng):
+    """Inputs of one verify sweep for the oracle port: x per (M, K), one packed
+    weight per shape (random codes; scale 2^-7 and bias -2^-6 per group)."""
     import numpy as np
 
-    from oracle import gen, qmm
+    from oracle import gen
 
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    tot_b, tot_t = 0, 0.0
+    xs = {(m, k): gen.x_bf16(rng, m, k) for m in SWEEP_M for k in {k for _, k in SHAPES}}
+    ws = {}
     for (n, k) in SHAPES:
-        x = gen.x_bf16(rng, 16, k)
         wq = rng.integers(0, 2**32, size=(n, k // 8), dtype=np.uint64).astype(np.uint32)
         s = np.full((n, k // 64), 0x3C00, dtype=np.uint16)  # bf16 0.0078125
         b = np.full((n, k // 64), 0xBC80, dtype=np.uint16)
-        qmm.qmm_cpu(x[:1], wq[:256], s[:256], b[:256], threads)  # warm
-        t0 = time.perf_counter()
-        qmm.qmm_cpu(x, wq, s, b, threads)
-        tot_t += time.perf_counter() - t0
-        tot_b += alg_bytes(16, n, k)
-    return {"value": round(tot_b / tot_t / 1e12, 6), "unit": UNIT, "cores": threads, "cpu_model": cpu_model(),
-            "kind": "port", "sample": "oracle port (dequantize + f32 matmul), one M=16 call on each of the 3 shapes"}
+        ws[(n, k)] = (wq, s, b)
+    return xs, ws
+
+
+def _cpu_sweep(xs, ws, threads):
+    """One step of the headline workload on the host: the 15 calls of the sweep,
+    each dequantizing its weight and multiplying (the reference's per-call
+    arithmetic). Returns (algorithmic bytes, seconds)."""
+    from oracle import qmm
+
+    tot_b, t0 = 0, time.perf_counter()
+    for m in SWEEP_M:
+        for (n, k) in SHAPES:
+            qmm.qmm_cpu(xs[(m, k)], *ws[(n, k)], threads)
+            tot_b += alg_bytes(m, n, k)
+    return tot_b, time.perf_counter() - t0
+
+
+CPU_SAMPLE = ("oracle port of the reference arithmetic (per call: dequantize the packed weight, f32 matmul), "
+              "the full 15-call verify sweep per step, row blocks over all host threads")
+
+
+def cpu_baseline_sample():
+    """The oracle port on this host's cores: one full sweep (after a small warm call)."""
+    import numpy as np
+
+    from oracle import qmm
+
+    threads = os.cpu_count() or 1
+    xs, ws = _cpu_sweep_data(np.random.default_rng(0))
+    (n0, k0) = SHAPES[0]
+    qmm.qmm_cpu(xs[(1, k0)], *(a[:256] for a in ws[(n0, k0)]), threads)  # warm the thread pool
+    tot_b, dt = _cpu_sweep(xs, ws, threads)
+    return {"value": round(tot_b / dt / 1e12, 6), "unit": UNIT, "cores": threads, "cpu_model": cpu_model(),
+            "kind": "port", "sample": CPU_SAMPLE + f"; one step, {dt:.1f} s"}
 
 
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args):
-    """The reference's algorithm on the host CPU (oracle port), rank 0 only."""
+    """The reference's algorithm on the host CPU (oracle port), rank 0 only:
+    the same 15-call sweep per step as the GPU arm."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import numpy as np
 
-    from oracle import gen, qmm
-
     threads = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    # one M = 16 call per step, cycling through the three shapes
-    data = []
-    for (n, k) in SHAPES:
-        x = gen.x_bf16(rng, 16, k)
-        wq = rng.integers(0, 2**32, size=(n, k // 8), dtype=np.uint64).astype(np.uint32)
-        s = np.full((n, k // 64), 0x3C00, dtype=np.uint16)
-        b = np.full((n, k // 64), 0xBC80, dtype=np.uint16)
-        data.append((x, wq, s, b, alg_bytes(16, n, k)))
-    for i in range(args.warmup):
-        x, wq, s, b, _ = data[i % 3]
-        qmm.qmm_cpu(x, wq, s, b, threads)
-    tot_b, t0 = 0, time.perf_counter()
-    for i in range(args.steps):
-        x, wq, s, b, nb = data[i % 3]
-        qmm.qmm_cpu(x, wq, s, b, threads)
-        tot_b += nb
-    dt = time.perf_counter() - t0
+    xs, ws = _cpu_sweep_data(np.random.default_rng(0))
+    # one untimed sweep warms the host (page faults, thread pool): more would
+    # only lengthen a run whose steps take seconds each
+    for _ in range(min(args.warmup, 1)):
+        _cpu_sweep(xs, ws, threads)
+    tot_b, dt = 0, 0.0
+    for _ in range(args.steps):
+        b_, t_ = _cpu_sweep(xs, ws, threads)
+        tot_b += b_
+        dt += t_
     value = tot_b / dt / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "verify-pass qmm sweep (bounded sample: one M=16 call per step, shapes cycled)",
+        "config": {"workload": WORKLOAD, "bytes_per_step": sum(alg_bytes(m, n, k) for m in SWEEP_M for (n, k) in SHAPES),
+                   "calls_per_step": len(SWEEP_M) * len(SHAPES),
                    "note": "reference kernels are Metal (MLX/MTPLX), unavailable on this box; "
-                           "CPU port of its arithmetic"},
+                           "CPU port of its arithmetic; warm-up capped at one sweep"},
         "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "cpu_model": cpu_model(),
-                         "kind": "port", "sample": "one M=16 qmm per step over the 3 shapes (dequantize + f32 matmul)"},
+                         "kind": "port", "sample": CPU_SAMPLE},
         "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
