@@ -85,6 +85,10 @@ int tsb_device_status(tsb_stream_t stream, int reset);
  * Requirements: M >= 1, N % 128 == 0, K % 64 == 0, ldy % 8 == 0; x, w, y
  * 16-byte aligned. Accumulation in float32. Declines (TSB_EUNSUPPORTED)
  * other N/K granularities.
+ * Routing by M (the reference's packed_linear._call, packed_linear.py:10-13,
+ * 83-104): M <= 2 a CUDA-core GEMV (x staged in shared memory; past its size
+ * the verify kernel), M <= 128 the tcgen05 verify kernel, larger M the
+ * tcgen05 prefill GEMM.
  *
  * Workspace (M <= 128, the verify path): tsb_qmm_workspace_bytes(M, N, K)
  * bytes, 256-byte aligned, computed for the current device. It holds
@@ -118,9 +122,9 @@ int tsb_qmm_w4g64(const void *x, const uint32_t *w, const void *scales, const vo
  * TSB_ETIMEOUT (tsb_device_status). Before storing into a peer's y, a call
  * waits until that peer has started the same call, so work queued before it
  * on the peer's stream (readers of the old contents) has finished.
- * Any M: M <= 128 runs the verify kernel, larger M the prefill GEMM, each
- * storing its tiles into every rank's y as they complete (the transfer overlaps
- * the matmul). ldy >= world*Ns; workspace tsb_qmm_workspace_bytes(M, Ns, K)
+ * Any M: M <= 2 runs the GEMV, M <= 128 the verify kernel, larger M the
+ * prefill GEMM, each storing its outputs into every rank's y as they complete
+ * (the transfer overlaps the matmul). ldy >= world*Ns; workspace tsb_qmm_workspace_bytes(M, Ns, K)
  * (none past M = 128); other rules as tsb_qmm_w4g64.
  * ---------------------------------------------------------------------- */
 #define TSB_MAX_GATHER_RANKS 8
