@@ -597,7 +597,7 @@ struct TsPlan {
 template <int NP>
 TsPlan plan_ts(int M, int N, int K) {
   (void)M;
-  const SkPlan sk = plan_stream_k(N, K);
+  const SkPlan sk = plan_stream_k(N, K, NP == 128);
   TsPlan p;
   p.U = sk.U;
   p.P = sk.P;
