@@ -25,7 +25,7 @@
 // (tree_flash.py:14-19,86-100): a key's scale multiplies its scores, a value's
 // scale the softmax weight it meets; running sums use the unscaled weights.
 // MLX_Q8_G64 rows are dequantized (s * q + b, rounded to bf16) into the tile.
-#include "common.cuh"
+#include "sm100.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -409,6 +409,8 @@ __global__ void __launch_bounds__(256) tree_attn_combine_kernel(const float *__r
                                                                 const float *__restrict__ part_ml, int splits,
                                                                 int rows, uint16_t *__restrict__ out,
                                                                 float *__restrict__ lse) {
+  griddep_wait();  // launched as a programmatic dependent: the partials are the attention kernel's
+  griddep_launch_dependents();
   __shared__ float sw[CB_ROWS][CB_MAX_SPLITS];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * CB_ROWS;
@@ -470,8 +472,8 @@ __global__ void __launch_bounds__(256) tree_attn_combine_kernel(const float *__r
 
 void launch_combine(const float *part_o, const float *part_ml, int splits, int rows, void *out, float *lse,
                     cudaStream_t st) {
-  tree_attn_combine_kernel<<<(unsigned)((rows + CB_ROWS - 1) / CB_ROWS), 256, 0, st>>>(
-      part_o, part_ml, splits, rows, (uint16_t *)out, lse);
+  launch_pdl(tree_attn_combine_kernel, dim3((unsigned)((rows + CB_ROWS - 1) / CB_ROWS)), dim3(256), 0, st, part_o,
+             part_ml, splits, rows, (uint16_t *)out, lse);
 }
 
 struct AttnPlan {

@@ -176,6 +176,10 @@ tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_con
   unsigned long long *sBits = reinterpret_cast<unsigned long long *>(bars + C::NBARS + 1);  // [T <= 64]
   int32_t *sPar = reinterpret_cast<int32_t *>(sBits + 64);                                 // [T <= 64]
 
+  // Launched as a programmatic dependent: q and the new K/V rows are the
+  // previous kernels'. Its own dependents (the split combine) launch as its
+  // CTAs exit: an early trigger would park their CTAs beside this kernel's.
+  griddep_wait();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int G = a.Hq / a.Hkv;
   const int R = G * a.T;
@@ -696,8 +700,8 @@ int launch_fmt(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &
     attr_dev = dev;
   }
   const dim3 grid(a.B * a.Hkv * a.row_blocks, a.splits);
-  tree_attn_tc_kernel<FMT><<<grid, C::THREADS, C::SMEM, st>>>(tq, tk, tv, a);
-  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+  const cudaError_t e = launch_pdl(tree_attn_tc_kernel<FMT>, grid, dim3(C::THREADS), (size_t)C::SMEM, st, tq, tk, tv, a);
+  return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 }  // namespace

@@ -15,7 +15,7 @@
 //
 // All of these move a few MB per layer at the verify step's M = B*T <= 128
 // rows: HBM-bound, vectorised 16-byte loads and stores, one launch each.
-#include "common.cuh"
+#include "sm100.cuh"
 
 namespace tsb {
 namespace {
@@ -45,6 +45,8 @@ TSB_HD uint4 pack8(const float (&f)[8]) {
 __global__ void __launch_bounds__(NORM_MAX_THREADS)
 add_rms_norm_kernel(const uint16_t *x, const uint16_t *r, const uint16_t *w, uint16_t *h_out, uint16_t *n_out, int D,
                     float eps) {
+  griddep_wait();  // launched as a programmatic dependent: inputs and outputs are the previous kernels'
+  griddep_launch_dependents();
   const size_t base = (size_t)blockIdx.x * D;
   const int nv = D / 8;
   const int nt = blockDim.x;
@@ -192,6 +194,8 @@ constexpr int PREP_THREADS = 256;
 
 // One CTA per node: each warp takes head rows (queries, keys, values) in turn.
 __global__ void __launch_bounds__(PREP_THREADS) qkv_prep_kernel(PrepArgs a) {
+  griddep_wait();  // launched as a programmatic dependent: inputs and outputs are the previous kernels'
+  griddep_launch_dependents();
   const int m = blockIdx.x;  // node = request * T + t
   const int b = m / a.T, t = m - b * a.T;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -234,6 +238,8 @@ __global__ void __launch_bounds__(PREP_THREADS) qkv_prep_kernel(PrepArgs a) {
 // qkv[b*T + t, h*512 + 256 + d]: o_proj's input (tree_verify.py:327).
 __global__ void attn_gate_kernel(const uint16_t *out, const uint16_t *qkv, int ld, uint16_t *y, int T, int Hq,
                                  size_t n_vec) {
+  griddep_wait();  // launched as a programmatic dependent: inputs and outputs are the previous kernels'
+  griddep_launch_dependents();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // 16-byte vector of y
   if (i >= n_vec) return;
   const int per_row = Hq * 32;  // vectors per y row
@@ -251,6 +257,8 @@ __global__ void attn_gate_kernel(const uint16_t *out, const uint16_t *qkv, int l
 
 // y[m, i] = bf16(bf16(g * bf16(sigmoid(g))) * u), g = gu[m, i], u = gu[m, I + i].
 __global__ void swiglu_kernel(const uint16_t *gu, uint16_t *y, int I, size_t n_vec) {
+  griddep_wait();  // launched as a programmatic dependent: inputs and outputs are the previous kernels'
+  griddep_launch_dependents();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_vec) return;
   const int per_row = I / 8;
@@ -280,9 +288,10 @@ extern "C" int tsb_add_rms_norm(const void *x, const void *r, const void *w, voi
   // one thread per 16-byte vector, in whole warps; beyond 1024 vectors, two each
   const int nv = D / 8;
   const int threads = nv <= NORM_MAX_THREADS ? (nv + 31) / 32 * 32 : NORM_MAX_THREADS;
-  add_rms_norm_kernel<<<rows, threads, 0, (cudaStream_t)stream>>>(
-      (const uint16_t *)x, (const uint16_t *)r, (const uint16_t *)w, (uint16_t *)h_out, (uint16_t *)n_out, D, eps);
-  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+  const cudaError_t e = launch_pdl(add_rms_norm_kernel, dim3(rows), dim3(threads), 0, (cudaStream_t)stream,
+                                   (const uint16_t *)x, (const uint16_t *)r, (const uint16_t *)w, (uint16_t *)h_out,
+                                   (uint16_t *)n_out, D, eps);
+  return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 extern "C" int tsb_qkv_prep(const void *qkv, int ld, int B, int T, int Hq, int Hkv, int D, const void *q_norm,
@@ -319,8 +328,8 @@ extern "C" int tsb_qkv_prep(const void *qkv, int ld, int B, int T, int Hq, int H
   a.offsets = offsets;
   a.k = k; a.v = v;
   a.ks = k_scales; a.kb = k_biases; a.vs = v_scales; a.vb = v_biases;
-  qkv_prep_kernel<<<B * T, PREP_THREADS, 0, (cudaStream_t)stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+  const cudaError_t e = launch_pdl(qkv_prep_kernel, dim3(B * T), dim3(PREP_THREADS), 0, (cudaStream_t)stream, a);
+  return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 extern "C" int tsb_attn_gate(const void *attn_out, const void *qkv, int ld, void *y, int B, int T, int Hq, int D,
@@ -331,9 +340,10 @@ extern "C" int tsb_attn_gate(const void *attn_out, const void *qkv, int ld, void
   if ((long long)ld < (long long)2 * Hq * D || ld % 8) return TSB_EINVAL;
   if (!aligned(attn_out, 16) || !aligned(qkv, 16) || !aligned(y, 16)) return TSB_EINVAL;
   const size_t n_vec = (size_t)B * T * Hq * (D / 8);
-  attn_gate_kernel<<<(unsigned)((n_vec + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      (const uint16_t *)attn_out, (const uint16_t *)qkv, ld, (uint16_t *)y, T, Hq, n_vec);
-  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+  const cudaError_t e = launch_pdl(attn_gate_kernel, dim3((unsigned)((n_vec + 255) / 256)), dim3(256), 0,
+                                   (cudaStream_t)stream, (const uint16_t *)attn_out, (const uint16_t *)qkv, ld,
+                                   (uint16_t *)y, T, Hq, n_vec);
+  return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
 extern "C" int tsb_swiglu(const void *gate_up, void *y, int M, int I, tsb_stream_t stream) {
@@ -342,7 +352,7 @@ extern "C" int tsb_swiglu(const void *gate_up, void *y, int M, int I, tsb_stream
   if (I % 8) return TSB_EUNSUPPORTED;
   if (!aligned(gate_up, 16) || !aligned(y, 16)) return TSB_EINVAL;
   const size_t n_vec = (size_t)M * (I / 8);
-  swiglu_kernel<<<(unsigned)((n_vec + 255) / 256), 256, 0, (cudaStream_t)stream>>>((const uint16_t *)gate_up,
-                                                                                   (uint16_t *)y, I, n_vec);
-  return cudaGetLastError() == cudaSuccess ? TSB_OK : TSB_ECUDA;
+  const cudaError_t e = launch_pdl(swiglu_kernel, dim3((unsigned)((n_vec + 255) / 256)), dim3(256), 0,
+                                   (cudaStream_t)stream, (const uint16_t *)gate_up, (uint16_t *)y, I, n_vec);
+  return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }

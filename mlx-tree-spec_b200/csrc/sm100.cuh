@@ -107,6 +107,27 @@ TSB_HD void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_de
 // visible (returns at once for a kernel launched without the attribute).
 TSB_HD void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Launch `kernel` with programmatic stream serialization: it may be scheduled
+// while the previous kernel of the stream is still running, so it must call
+// griddep_wait() before it touches memory that earlier kernels of the stream
+// write or read (the small kernels below do so first thing, then let their own
+// dependents launch; the matmuls stream their constant weights before waiting).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
 // ---------------------------------------------------------------- TMA
 TSB_HD void tma_prefetch_desc(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
