@@ -184,11 +184,6 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
   };
   const int first_loads = L < C::NC ? L : C::NC;
 
-  if (threadIdx.x == 0) {
-    // the next kernel on the stream may start its CTAs as this one's exit (it
-    // waits for this grid before touching anything this grid writes)
-    griddep_launch_dependents();
-  }
   if (warp == C::CODES_WARP && lane == 0) {
     for (int s = 0; s < C::NC; ++s) {
       mbar_init(&full_c[s], 1);
@@ -239,6 +234,11 @@ qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant_
         issue_codes(li, ring.slot);
         issued = li + 1;
       }
+      // the next kernel on the stream may start its CTAs once every CTA here
+      // has issued its last weight load (it waits for this grid before
+      // touching anything this grid writes); triggering at the start parked
+      // the small decoder kernels' CTAs beside this one for its whole run
+      griddep_launch_dependents();
       // drain: every issued load has landed before the CTA can exit
       for (int i = (issued > C::NC ? issued - C::NC : 0); i < issued; ++i) {
         const unsigned long long t0 = globaltimer_ns();
