@@ -58,11 +58,12 @@ def test_qmm_config1_seed0():
     assert_close_rel(y, ref, REL_TIGHT, "config1")
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 16, 31, 32, 64, 65, 128])
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 16, 31, 32, 33, 48, 64, 65, 128])
 @pytest.mark.parametrize("nk", [(6144, 5120), (34816, 5120), (5120, 17408)])
 def test_qmm_sweep_sampled_rows(m, nk):
-    """The sweep shapes at every sweep M (plus odd M); the oracle is
-    evaluated on a seeded sample of 384 output rows (all of K)."""
+    """The sweep shapes at every sweep M (plus odd M; 33-64 on 34816x5120 run the
+    verify kernel's whole-tile configuration, the other shapes its default);
+    the oracle is evaluated on a seeded sample of 384 output rows (all of K)."""
     import tsb
 
     n, k = nk
