@@ -72,12 +72,18 @@ namespace tsb {
 
 namespace {
 
-// WHOLE: the call's CTAs stream whole row tiles (more tiles than SMs), used at
-// NP = 64 only: four MMA issuers with two stage slots instead of two issuers
-// with three. Measured on B200 at M = 33-64: 8-10% faster on 34816x5120, but
-// 3-11% slower on 6144x5120 and mixed on 5120x17408, whose CTAs hold parts of
-// tiles, so those keep the default.
-template <int NP, bool WHOLE = false>
+// Configuration variants (VAR), chosen per call by qmm_ts():
+//   kTsDefault;
+//   kTsWhole (NP = 64, the call's CTAs stream whole row tiles: more tiles than
+//     SMs): four MMA issuers with two stage slots instead of two issuers with
+//     three. Measured on B200 at M = 33-64: 8-10% faster on 34816x5120, but
+//     3-11% slower on 6144x5120 and mixed on 5120x17408, which keep the default;
+//   kTsShort (NP = 128, every CTA's range at most 10 stages): one issuer with
+//     three stage slots instead of two with two: ~1 us faster on 6144x5120 and
+//     5120x6144 (7-8 stages per CTA), 3-5 us slower on longer ranges.
+constexpr int kTsDefault = 0, kTsWhole = 1, kTsShort = 2;
+
+template <int NP, int VAR = kTsDefault>
 struct TsCfg {
   static constexpr int ROWS = 128;
   static constexpr int SG = 4;                     // groups per stage
@@ -90,8 +96,9 @@ struct TsCfg {
   // dequantizer warpgroups = A stage slots; at NP = 128 two, so that TMEM holds
   // a second accumulator: one thread issues at most one M=128 K=16 MMA per
   // ~68 ns whatever N is, so a single issuer would bound a stage at ~1.1 us
-  static constexpr int WGS = (NP == 128 || WHOLE) ? 2 : 3;
-  static constexpr int NI = (NP <= 32 || WHOLE) ? 4 : 2;  // MMA issuers, one accumulator each
+  static constexpr int WGS = NP == 128 ? (VAR == kTsShort ? 3 : 2) : (VAR == kTsWhole ? 2 : 3);
+  static constexpr int NI = NP == 128 ? (VAR == kTsShort ? 1 : 2)                 // MMA issuers,
+                                      : ((NP <= 32 || VAR == kTsWhole) ? 4 : 2);  // one accumulator each
   static constexpr int GPI = SG / NI;              // groups per issuer
   static constexpr int NX = NP <= 32 ? 4 : (NP == 64 ? 3 : 2);  // x slots
   static constexpr int NC_FIT = (RING_BUDGET - NX * XSLOT_BYTES) / CSLOT_BYTES;
@@ -130,11 +137,11 @@ struct TsArgs {
   uint32_t *sig[kMaxGatherRanks];
 };
 
-template <int NP, bool WHOLE>
-__global__ void __launch_bounds__(TsCfg<NP, WHOLE>::THREADS, 1)
+template <int NP, int VAR>
+__global__ void __launch_bounds__(TsCfg<NP, VAR>::THREADS, 1)
 qmm_ts_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
               const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_b, TsArgs a) {
-  using C = TsCfg<NP, WHOLE>;
+  using C = TsCfg<NP, VAR>;
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -614,10 +621,10 @@ TsPlan plan_ts(int M, int N, int K) {
   return p;
 }
 
-template <int NP, bool WHOLE = false>
+template <int NP, int VAR = kTsDefault>
 int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16_t *b, uint16_t *y, int M, int N,
               int K, int ldy, void *ws, size_t ws_bytes, const GatherSpec *gs, cudaStream_t st) {
-  using C = TsCfg<NP, WHOLE>;
+  using C = TsCfg<NP, VAR>;
   const TsPlan plan = plan_ts<NP>(M, N, K);
   if ((size_t)plan.tiles * plan.maxp * sizeof(uint32_t) > kFlagRegionBytes) return TSB_EUNSUPPORTED;
   if (!ws || ws_bytes < plan.flag_bytes + plan.part_bytes) return TSB_EWORKSPACE;
@@ -645,7 +652,7 @@ int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uin
   int dev = 0;
   cudaGetDevice(&dev);
   if (attr_dev != dev) {
-    if (cudaFuncSetAttribute(qmm_ts_kernel<NP, WHOLE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) !=
+    if (cudaFuncSetAttribute(qmm_ts_kernel<NP, VAR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM) !=
         cudaSuccess)
       return TSB_ECUDA;
     attr_dev = dev;
@@ -688,7 +695,7 @@ int launch_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uin
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_ts_kernel<NP, WHOLE>, tx, tw, tsc, tbi, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qmm_ts_kernel<NP, VAR>, tx, tw, tsc, tbi, a);
   return e == cudaSuccess ? TSB_OK : TSB_ECUDA;
 }
 
@@ -712,9 +719,11 @@ int qmm_ts(const uint16_t *x, const uint32_t *w, const uint16_t *s, const uint16
   if (M <= 32) return launch_ts<32>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
   if (M <= 64) {
     if (plan_ts<64>(M, N, K).tiles > sm_count())
-      return launch_ts<64, true>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
+      return launch_ts<64, kTsWhole>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
     return launch_ts<64>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
   }
+  const TsPlan p = plan_ts<128>(M, N, K);
+  if ((p.U + p.P - 1) / p.P <= 10) return launch_ts<128, kTsShort>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
   return launch_ts<128>(x, w, s, b, y, M, N, K, ldy, ws, ws_bytes, gs, st);
 }
 
