@@ -71,8 +71,29 @@ def qmm_workspace(nbytes: int, device) -> torch.Tensor:
     return buf
 
 
+# The raw current-stream handle: torch's own C++ accessor when this build of
+# torch has it (a fraction of the ~2 us that torch.cuda.current_stream() costs
+# per call, which matters for M = 1 calls of a few microseconds), else the
+# public API.
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(t: torch.Tensor) -> int:
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+_QWS_BYTES: dict[tuple, int] = {}
+
+
+def _qmm_ws_bytes(lib, m: int, n: int, k: int, dev: int) -> int:
+    """tsb_qmm_workspace_bytes, remembered per (M, N, K, device) on the host side."""
+    key = (m, n, k, dev)
+    v = _QWS_BYTES.get(key)
+    if v is None:
+        v = _QWS_BYTES[key] = lib.tsb_qmm_workspace_bytes(m, n, k)
+    return v
 
 
 def _ptr(t):
@@ -108,7 +129,7 @@ def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: i
     if out is None:
         out = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=x.device)
     lib = _lib.load()
-    ws = qmm_workspace(lib.tsb_qmm_workspace_bytes(m, n, k), x.device)
+    ws = qmm_workspace(_qmm_ws_bytes(lib, m, n, k, x.device.index), x.device)
     st = lib.tsb_qmm_w4g64(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(out), m, n, k, n,
                            _ptr(ws), ws.numel(), _stream(x))
     if check(st, "tsb_qmm_w4g64") == TSB_EUNSUPPORTED:
@@ -123,7 +144,7 @@ def quantized_matmul_into(x2, w, scales, biases, y, ldy: int):
     m, k = x2.shape
     n = w.shape[0]
     lib = _lib.load()
-    ws = qmm_workspace(lib.tsb_qmm_workspace_bytes(m, n, k), x2.device)
+    ws = qmm_workspace(_qmm_ws_bytes(lib, m, n, k, x2.device.index), x2.device)
     st = lib.tsb_qmm_w4g64(_ptr(x2), _ptr(w), _ptr(scales), _ptr(biases), _ptr(y), m, n, k, ldy,
                            _ptr(ws), ws.numel(), _stream(x2))
     return check(st, "tsb_qmm_w4g64")
